@@ -1,0 +1,587 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 sparse-KV residency data path.
+
+Headline: Top-K K/V row gather from a VMM-backed
+pool of 36 layers x K,V planes [262144, 8, 128] bf16 (36 GiB), 64 requests x
+2048 Top-K slots, all 72 planes in one launch of the sm_100a gather kernel
+(index chain positions -> request_table -> slot_offsets resolved per row).
+Under ``--gpus N`` (torchrun) the KV heads are sharded across ranks
+(tensor-parallel layout: 8/N heads per rank, same slots), so the total work is
+fixed: ``scaling = strong``.  One step = one launch over the whole batch.
+
+Extra keys: ``e2e`` (public Python API per step, positions copied from pinned
+host memory and one result row read back), ``roofline`` (gather kernel vs the
+measured HBM copy peak), ``cpu_baseline`` (torch-CPU restatement on the host
+cores, bounded sample), ``migration`` (config 3: 256 victim chunks packed into
+2 MiB-aligned pinned staging and restored into fresh VMM chunks with permuted
+slots; host-link GB/s per direction), ``bitmap`` (config 4 geometry: freeable
+bitmap build and the NCCL AND-combine latency), ``clocks`` (NVML samples
+during the timed region).
+
+``--impl reference`` times the reference's CPU path (torch-CPU restatement,
+all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _path in (str(ROOT / "elastic-kv-vmm_b200"), str(ROOT)):
+    if _path not in sys.path:
+        sys.path.insert(0, _path)
+
+import torch  # noqa: E402
+
+CHUNK = 2 << 20
+CFG2 = dict(layers=36, kv_heads=8, head_dim=128, slots=262144, requests=64, topk=2048)
+INDEX_BYTES_PER_ROW_PAIR = 4  # per-unit index bytes of the algorithmic byte count
+METRIC = "Top-K KV rows/s (gather, row-pairs/s)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--layers", type=int, default=CFG2["layers"],
+                   help="layers in the pool (36 = config 2; smaller only for profiling captures)")
+    p.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--skip-migration", action="store_true")
+    p.add_argument("--skip-e2e", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
+    return p.parse_args(argv)
+
+
+# --------------------------------------------------------------------------- plumbing
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.enabled = self.world > 1
+        if self.enabled:
+            import datetime
+
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local_rank))
+        self.device = torch.device("cuda", self.local_rank)
+        torch.cuda.set_device(self.device)
+
+    def barrier(self):
+        if self.enabled:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[self.local_rank])
+
+    def max(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        import torch.distributed as dist
+
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.enabled:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+def measured_hbm_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback (profiling recipe 6.65 TB/s)"
+
+
+class ClockSampler:
+    """NVML samples of SM clock and clock-event reasons while the region runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks",
+               0x10: "sync_boost", 0x100: "display_clocks"}
+
+    def __init__(self, index: int, period: float = 0.02):
+        self.samples = []
+        self.reasons = set()
+        self.period = period
+        self._stop = threading.Event()
+        self._thread = None
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: report no clocks rather than guess
+            self._nvml = None
+
+    def _reasons_now(self):
+        nvml = self._nvml
+        getter = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        return int(getter(self._handle))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nvml.nvmlDeviceGetClockInfo(self._handle, self._nvml.NVML_CLOCK_SM))
+                bits = self._reasons_now()
+                for bit, name in self.REASONS.items():
+                    if bits & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def timed(fn, steps, warmup, dist: Dist):
+    """Device time (ms, max over ranks) of `steps` calls after `warmup` calls."""
+    for _ in range(warmup):
+        fn()
+    stream = torch.cuda.current_stream()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return dist.max(start.elapsed_time(end))
+
+
+# --------------------------------------------------------------------------- workload
+
+class Workload:
+    """Config-2 pool (VMM-backed) and Top-K indices for this rank's head shard."""
+
+    def __init__(self, dist: Dist, layers: int):
+        from ekv_b200.backing import Backing
+        from ekv_b200.virtual_layout import VirtualKVLayout
+
+        if CFG2["kv_heads"] % dist.world:
+            raise SystemExit("--gpus must divide the 8 KV heads")
+        self.dist = dist
+        dev = dist.device
+        self.layers = layers
+        self.heads = CFG2["kv_heads"] // dist.world
+        self.width = self.heads * CFG2["head_dim"]             # elements per row (this rank)
+        self.row_bytes = self.width * 2
+        self.slots = CFG2["slots"]
+        self.n_planes = 2 * layers
+        self.plane_bytes = self.slots * self.row_bytes
+        self.plane_chunks = -(-self.plane_bytes // CHUNK)
+        capacity = CHUNK * (1 + self.n_planes * self.plane_chunks)
+        started = time.perf_counter()
+        self.backing = Backing(capacity, CHUNK, device=dev.index)
+        self.backing.ensure(range(1 + self.n_planes * self.plane_chunks))
+        self.map_seconds = time.perf_counter() - started
+        raw = self.backing.raw
+        gen = torch.Generator(device=dev).manual_seed(1234 + dist.rank)
+        self.planes = []
+        for p in range(self.n_planes):
+            start = CHUNK * (1 + p * self.plane_chunks)
+            plane = raw[start:start + self.plane_bytes].view(torch.bfloat16).view(
+                self.slots, self.heads, CFG2["head_dim"])
+            torch.randn(plane.shape, generator=gen, dtype=torch.bfloat16, device=dev, out=plane)
+            self.planes.append(plane)
+        del raw
+        b, k = CFG2["requests"], CFG2["topk"]
+        igen = torch.Generator(device=dev).manual_seed(42)  # same indices on every rank
+        self.request_table = torch.stack([torch.randperm(self.slots, generator=igen, device=dev)[:k]
+                                          for _ in range(b)])
+        self.positions = torch.stack([torch.randperm(k, generator=igen, device=dev) for _ in range(b)])
+        self.request_ids = torch.arange(b, device=dev)
+        self.lengths = torch.full((b,), k, dtype=torch.int64, device=dev)
+        self.slot_offsets = torch.arange(self.slots, dtype=torch.int64, device=dev) * self.width
+        self.layout = VirtualKVLayout(b, k, self.width)
+        self.outputs = [torch.empty((b, k, self.heads, CFG2["head_dim"]), dtype=torch.bfloat16, device=dev)
+                        for _ in range(self.n_planes)]
+        self.rows = b * k                                  # row-pairs per layer
+        self.units = self.rows * layers                    # row-pairs per step (whole job)
+        torch.cuda.synchronize()
+
+    def plane_gather(self):
+        from ekv_b200.sparse_read import PlaneGather
+
+        return PlaneGather([p.view(self.slots, self.width) for p in self.planes], self.positions,
+                           self.request_ids, self.lengths, self.request_table, self.slot_offsets,
+                           [o.view(o.shape[0], o.shape[1], self.width) for o in self.outputs],
+                           self.layout, indirect=True)
+
+    def close(self):
+        self.planes = self.outputs = None
+        torch.cuda.synchronize()
+        self.backing.close()
+
+
+def algorithmic_bytes_per_row_pair(row_bytes: int) -> int:
+    """Read K and V rows, write K and V rows, plus the per-unit index bytes."""
+    return 4 * row_bytes + INDEX_BYTES_PER_ROW_PAIR
+
+
+def traffic_per_launch(units: int, row_bytes: int):
+    """DRAM bytes per launch from the committed ncu summary (scaled per row-pair)."""
+    path = ROOT / "profiles" / "gather_kernel_cfg2.md"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("dram_bytes_per_row_pair_2048B:"):
+                per_unit = float(line.split(":", 1)[1])
+                return per_unit * units * (row_bytes / 2048.0)
+    except OSError:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------------- CPU legs
+
+def cpu_sample(work: Workload, layers: int):
+    """Host copies of `layers` layers of the pool plus the indices (the bounded sample)."""
+    planes = [work.planes[p].view(work.slots, work.width).view(torch.int16).cpu()
+              for p in range(2 * layers)]
+    idx = dict(positions=work.positions.cpu(), request_ids=work.request_ids.cpu(),
+               lengths=work.lengths.cpu(), request_table=work.request_table.cpu(),
+               slot_offsets=work.slot_offsets.cpu())
+    outputs = [torch.empty((work.rows // CFG2["topk"], CFG2["topk"], work.width), dtype=torch.int16)
+               for _ in planes]
+    return planes, idx, outputs
+
+
+def run_cpu_gather(planes, idx, outputs, width):
+    from oracle.cpu_baseline import gather_planes
+
+    gather_planes(planes, idx["positions"], idx["request_ids"], idx["lengths"], idx["request_table"],
+                  idx["slot_offsets"], width, outputs)
+
+
+def cpu_baseline(work: Workload, seconds: float, sample_layers: int = 1):
+    """Time the torch-CPU restatement on all host threads for ~`seconds`; check parity."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    planes, idx, outputs = cpu_sample(work, sample_layers)
+    run_cpu_gather(planes, idx, outputs, work.width)  # warm-up + parity sample
+    parity = all(torch.equal(out, work.outputs[p].view(out.shape).view(torch.int16).cpu())
+                 for p, out in enumerate(outputs))
+    reps, started = 0, time.perf_counter()
+    while reps < 2 or time.perf_counter() - started < seconds:
+        run_cpu_gather(planes, idx, outputs, work.width)
+        reps += 1
+    elapsed = time.perf_counter() - started
+    units = reps * work.rows * sample_layers
+    return {"value": units / elapsed, "unit": "row-pairs/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_layers} of {work.layers} layers (K and V), all {work.rows} Top-K "
+                      f"row-pairs per layer, {reps} repetitions in {elapsed:.1f} s",
+            "cpu": platform.processor() or platform.machine(), "parity_with_gpu": parity}
+
+
+# --------------------------------------------------------------------------- migration (config 3)
+
+def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
+    from ekv_b200.host_pool import pack_rows, pinned_buffer, unpack_rows
+
+    dev = work.dist.device
+    gen = torch.Generator().manual_seed(7)
+    rows_per_chunk = CHUNK // work.row_bytes
+    victims = torch.randperm(work.n_planes * work.plane_chunks, generator=gen)[:victims_n]
+    plane_index, src, dst, stage = [], [], [], []
+    for v, victim in enumerate(victims.tolist()):
+        plane, chunk = divmod(victim, work.plane_chunks)
+        density = 0.5 + 0.5 * torch.rand((), generator=gen).item()
+        occupied = torch.nonzero(torch.rand(rows_per_chunk, generator=gen) < density).flatten()
+        perm = torch.randperm(rows_per_chunk, generator=gen)
+        plane_index.append(torch.full((occupied.numel(),), plane, dtype=torch.int32))
+        src.append(chunk * rows_per_chunk + occupied)
+        dst.append(chunk * rows_per_chunk + perm[occupied])
+        stage.append(v * rows_per_chunk + torch.arange(occupied.numel()))
+    plane_index = torch.cat(plane_index).to(dev)
+    src, dst, stage = torch.cat(src).to(dev), torch.cat(dst).to(dev), torch.cat(stage).to(dev)
+    n_rows = src.numel()
+    moved = n_rows * work.row_bytes
+    planes = [p.view(work.slots, work.row_bytes // 2).view(torch.uint8).view(work.slots, work.row_bytes)
+              for p in work.planes]
+    staging = pinned_buffer(victims_n * CHUNK).view(-1, work.row_bytes)
+    shadow = torch.empty((n_rows, work.row_bytes), dtype=torch.uint8, device=dev)
+    dense = torch.arange(n_rows, device=dev)
+    pack_rows(planes, src, shadow, plane_index=plane_index, stage_rows=dense)  # device copy for checking
+
+    def event_time(fn):
+        times = []
+        for _ in range(reps):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            start.record()
+            fn()
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end) / 1e3)
+        return min(times), statistics.median(times)
+
+    d2h_best, d2h_med = event_time(lambda: pack_rows(planes, src, staging, plane_index=plane_index,
+                                                     stage_rows=stage))
+    chunk_ids = {1 + int(v) for v in victims}
+    started = time.perf_counter()
+    work.backing.reclaim(chunk_ids)
+    reclaim_s = time.perf_counter() - started
+    started = time.perf_counter()
+    work.backing.ensure(chunk_ids)
+    ensure_s = time.perf_counter() - started
+    h2d_best, h2d_med = event_time(lambda: unpack_rows(planes, dst, staging, plane_index=plane_index,
+                                                       stage_rows=stage))
+    restored = torch.empty_like(shadow)
+    pack_rows(planes, dst, restored, plane_index=plane_index, stage_rows=dense)
+    torch.cuda.synchronize()
+    exact = bool(torch.equal(restored, shadow))
+    # Copy-engine reference on the same link: one contiguous pinned <-> device copy.
+    flat_host = staging.view(-1)[:moved]
+    flat_dev = torch.empty(moved, dtype=torch.uint8, device=dev)
+    ce_h2d, _ = event_time(lambda: flat_dev.copy_(flat_host, non_blocking=True))
+    ce_d2h, _ = event_time(lambda: flat_host.copy_(flat_dev, non_blocking=True))
+    gbs = lambda seconds: moved / seconds / 1e9  # noqa: E731
+    return {"victim_chunks": victims_n, "rows": n_rows, "bytes_per_direction": moved,
+            "d2h_gbs": gbs(d2h_best), "h2d_gbs": gbs(h2d_best),
+            "d2h_gbs_median": gbs(d2h_med), "h2d_gbs_median": gbs(h2d_med),
+            "copy_engine_d2h_gbs": gbs(ce_d2h), "copy_engine_h2d_gbs": gbs(ce_h2d),
+            "host_link_nominal_gbs": 64.0, "reclaim_ms": reclaim_s * 1e3, "ensure_ms": ensure_s * 1e3,
+            "round_trip_bit_exact": exact, "path": "pack/unpack kernel, zero-copy pinned staging"}
+
+
+# --------------------------------------------------------------------------- bitmap (config 4 geometry)
+
+def bitmap_bench(dist: Dist, reps: int = 50):
+    from ekv_b200.releasable import (ChunkProjection, bitmap_to_chunks, chunks_to_bitmap,
+                                     combine_freeable, freeable_bitmap)
+
+    dev = dist.device
+    layers, n_chunks = 48, 4096
+    row_bytes = 2048 // dist.world
+    planes_n = 2 * layers
+    per_plane = n_chunks // planes_n
+    slots = per_plane * CHUNK // row_bytes
+    planes = [(p * per_plane, row_bytes) for p in range(planes_n)]
+    # Every page (slot, page size 1) belongs to one of 32 requests; request 0
+    # owns the first eighth of the slots, so its pages hold whole chunks.
+    gen = torch.Generator().manual_seed(11)
+    owner = torch.randint(1, 32, (slots,), generator=gen)
+    owner[: slots // 8] = 0
+    projection = ChunkProjection(planes, 1, CHUNK, n_chunks, dev)
+    refs = projection.counts(torch.arange(slots, device=dev))
+    # Each rank has a few rank-specific unmapped chunks, so the AND is not trivial.
+    mapped_set = set(range(n_chunks)) - {(dist.rank * 37 + 5 * i) % n_chunks for i in range(8)}
+    mapped = chunks_to_bitmap(mapped_set, n_chunks, dev)
+    candidate = torch.nonzero(owner == 0).flatten().to(dev)
+
+    def build():
+        return freeable_bitmap(projection.counts(candidate), refs, mapped)
+
+    local = build()
+    joint = combine_freeable(local)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(reps):
+        build()
+    end.record(stream)
+    torch.cuda.synchronize()
+    build_ms = start.elapsed_time(end) / reps
+    dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(reps):
+        combine_freeable(local)
+    end.record(stream)
+    torch.cuda.synchronize()
+    combine_ms = dist.max(start.elapsed_time(end) / reps)
+    local_set = bitmap_to_chunks(local)
+    expected_joint = set(local_set)
+    for r in range(dist.world):
+        expected_joint -= {(r * 37 + 5 * i) % n_chunks for i in range(8)}
+    return {"chunks": n_chunks, "words": n_chunks // 64, "ranks": dist.world,
+            "freeable_local": len(local_set), "freeable_joint": len(bitmap_to_chunks(joint)),
+            "joint_matches_intersection": bitmap_to_chunks(joint) == expected_joint,
+            "build_us": build_ms * 1e3, "combine_us": combine_ms * 1e3,
+            "combine": "NCCL all_gather_into_tensor + AND kernel" if dist.world > 1 else "single rank"}
+
+
+# --------------------------------------------------------------------------- arms
+
+def run_ours(args, dist: Dist):
+    from ekv_b200.sparse_read import gather_rows_planes
+
+    work = Workload(dist, args.layers)
+    gather = work.plane_gather()
+    with ClockSampler(dist.local_rank) as clocks:
+        ms = timed(gather, args.steps, args.warmup, dist)
+    ms_per_step = ms / args.steps
+    value = work.units / (ms_per_step / 1e3)
+    peak, peak_source = measured_hbm_peak()
+    bytes_per_launch = work.units * algorithmic_bytes_per_row_pair(work.row_bytes)
+    achieved = bytes_per_launch / (ms_per_step / 1e3) / 1e9
+    rank_achieved = achieved  # per-GPU: every rank moves its own head shard
+    traffic = traffic_per_launch(work.units, work.row_bytes)
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "row-pairs/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 pool, seeded Top-K slots)",
+        "config": {"workload": f"config 2: sparse Top-K KV gather, {work.layers} layers x K,V, "
+                               f"pool [262144, 8, 128] bf16 per plane (VMM-backed), 64 requests x 2048 "
+                               f"Top-K, heads sharded {work.heads}/rank",
+                   "layers": work.layers, "requests": CFG2["requests"], "topk": CFG2["topk"],
+                   "slots": CFG2["slots"], "kv_heads_per_rank": work.heads, "row_bytes": work.row_bytes,
+                   "parallelism": f"tp{dist.world} (KV-head sharding, no data-path collective)",
+                   "l2": f"no flush: each step moves {bytes_per_launch / 1e9:.1f} GB per GPU (> 126 MB L2)"},
+        "hbm_gbs_per_gpu": achieved,
+        "roofline": {"bound": "hbm", "achieved": rank_achieved, "peak": peak, "unit": "GB/s",
+                     "frac": rank_achieved / peak, "traffic": traffic, "peak_source": peak_source,
+                     "kernel": "gather_kernel (ekv_gather_rows_planes)",
+                     "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "frac_of_nominal_8tbs": rank_achieved / 8000.0},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "vmm_map_seconds": work.map_seconds,
+    }
+
+    if not args.skip_e2e:
+        # End to end through the public API: positions H2D from pinned memory,
+        # gather_rows_planes (pointer tables rebuilt per call), one row read back.
+        pos_host = work.positions.cpu().pin_memory()
+        result_host = torch.empty(work.outputs[0][0, 0].shape, dtype=torch.bfloat16).pin_memory()
+        planes = [p.view(work.slots, work.width) for p in work.planes]
+        outs = [o.view(o.shape[0], o.shape[1], work.width) for o in work.outputs]
+
+        def e2e_step():
+            work.positions.copy_(pos_host, non_blocking=True)
+            gather_rows_planes(planes, work.positions, work.request_ids, work.lengths, work.request_table,
+                               work.slot_offsets, outs, work.layout, indirect=True)
+            result_host.copy_(work.outputs[0][0, 0], non_blocking=True)
+
+        e2e_steps = max(3, args.steps // 2)
+        ms_e2e = timed(e2e_step, e2e_steps, max(3, args.warmup), dist)
+        result["e2e"] = {"value": work.units / (ms_e2e / e2e_steps / 1e3), "unit": "row-pairs/s",
+                         "h2d_bytes_per_step": pos_host.numel() * pos_host.element_size(),
+                         "d2h_bytes_per_step": result_host.numel() * result_host.element_size(),
+                         "steps": e2e_steps, "ms_per_step": ms_e2e / e2e_steps,
+                         "api": "ekv_b200.sparse_read.gather_rows_planes (ctypes -> ekv_gather_rows_planes)"}
+        result["gpu_launches"] = args.steps  # the e2e loop is timed separately
+
+    result["bitmap"] = bitmap_bench(dist)
+
+    if dist.rank == 0 and dist.world == 1 and not args.skip_cpu:
+        result["cpu_baseline"] = cpu_baseline(work, args.cpu_seconds)
+    if dist.world == 1 and not args.skip_migration:
+        result["migration"] = migration_bench(work)
+    work.close()
+    return result
+
+
+def run_reference(args, dist: Dist):
+    """Reference arm: the torch-CPU restatement on the host cores, rank 0 only."""
+    if dist.rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(1234)
+    width = CFG2["kv_heads"] // dist.world * CFG2["head_dim"]
+    slots, b, k = CFG2["slots"], CFG2["requests"], CFG2["topk"]
+    sample_layers = 1
+    planes = [torch.randint(-32768, 32767, (slots, width), generator=gen, dtype=torch.int16)
+              for _ in range(2 * sample_layers)]
+    igen = torch.Generator().manual_seed(42)
+    idx = dict(request_table=torch.stack([torch.randperm(slots, generator=igen)[:k] for _ in range(b)]),
+               positions=torch.stack([torch.randperm(k, generator=igen) for _ in range(b)]),
+               request_ids=torch.arange(b), lengths=torch.full((b,), k, dtype=torch.int64),
+               slot_offsets=torch.arange(slots, dtype=torch.int64) * width)
+    outputs = [torch.empty((b, k, width), dtype=torch.int16) for _ in planes]
+    for _ in range(args.warmup):
+        run_cpu_gather(planes, idx, outputs, width)
+    started = time.perf_counter()
+    for _ in range(args.steps):
+        run_cpu_gather(planes, idx, outputs, width)
+    elapsed = time.perf_counter() - started
+    units = b * k * sample_layers
+    value = units * args.steps / elapsed
+    sample = (f"{sample_layers} of 36 layers (K and V planes [262144, {width}] bf16 bits), "
+              f"all {b * k} Top-K row-pairs per step")
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "row-pairs/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config 2 sample: sparse Top-K KV gather on the host cores",
+                   "layers_sampled": sample_layers, "requests": b, "topk": k,
+                   "parallelism": "cpu (all host threads)"},
+        "cpu_baseline": {"value": value, "unit": "row-pairs/s", "cores": threads, "kind": "port",
+                         "sample": sample, "cpu": platform.processor() or platform.machine()},
+        "e2e": {"value": value, "unit": "row-pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        from types import SimpleNamespace
+
+        world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+        result = run_reference(args, SimpleNamespace(rank=0, world=world))
+        print(json.dumps(result), flush=True)
+        return 0
+    dist = Dist()
+    try:
+        result = run_ours(args, dist)
+        if dist.rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

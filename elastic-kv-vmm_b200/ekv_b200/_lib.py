@@ -1,0 +1,181 @@
+"""ctypes binding of libekv_b200.so (include/ekv_kernels.h, include/ekv_vmm.h).
+
+The library is the only compute path: nothing here falls back to PyTorch or
+to the CPU.  If the shared object is missing, every kernel call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes as ct
+import functools
+import os
+from pathlib import Path
+
+import torch
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "lib" / "libekv_b200.so"
+MAX_PLANES = 256  # EKV_MAX_PLANES
+
+_p = ct.c_void_p
+_i32 = ct.c_int
+_i64 = ct.c_int64
+_u64p = ct.POINTER(ct.c_uint64)
+_i64p = ct.POINTER(ct.c_int64)
+
+# name -> argtypes (every kernel entry point returns int).
+_KERNELS = {
+    "ekv_resolve_resident": [
+        _p, _i32, _i64, _i64, _i64,
+        _p, _i32, _i64, _i64,
+        _p, _i32, _i64,
+        _p, _i32, _i64,
+        _p, _i32, _i64,
+        _p, _i32, _i64, _i64,
+        _p, _i64, _i64,
+        _i64, _i32, _p,
+    ],
+    "ekv_lookup_slots": [
+        _p, _i32, _i64, _i64,
+        _p, _i32, _i64,
+        _p, _i32,
+        _i64, _i64,
+        _p, _i64,
+        _p, _i64,
+        _p, _i64,
+        _p,
+        _i32, _p,
+    ],
+    "ekv_gather_rows": [
+        _p, _p, _i64,
+        _p, _i32, _p, _i32, _p, _i32, _p, _i32, _p, _i32,
+        _i64, _i64, _i64, _i64, _i64, _i64,
+        _i32, _i32, _p,
+    ],
+    "ekv_gather_rows_planes": [
+        _u64p, _u64p, _i32, _i64,
+        _p, _i32, _p, _i32, _p, _i32, _p, _i32, _p, _i32,
+        _i64, _i64, _i64, _i64, _i64, _i64,
+        _i32, _i32, _p,
+    ],
+    "ekv_pack_rows": [
+        _u64p, _i32, _i64,
+        _p, _p, _i32, _i64,
+        _p, _i32,
+        _p, _i64, _i64,
+        _i32, _p,
+    ],
+    "ekv_unpack_rows": [
+        _u64p, _i32, _i64,
+        _p, _p, _i32, _i64,
+        _p, _i32,
+        _p, _i64, _i64,
+        _i32, _p,
+    ],
+    "ekv_chunk_counts": [
+        _p, _i32, _i64,
+        _i64p, _i64p, _i32,
+        _i64, _i64,
+        _p, _i64, _i32, _p,
+        _i32, _p,
+    ],
+    "ekv_freeable_bitmap": [_p, _p, _p, _i64, _p, _i32, _p],
+    "ekv_bitmap_and": [_p, _i32, _i64, _p, _i32, _p],
+}
+
+_VMM = {
+    "ev_create": ([_i32, ct.c_uint64, ct.c_uint64], ct.c_void_p),
+    "ev_ensure": ([_p, _u64p, ct.c_size_t], ct.c_int),
+    "ev_precommit": ([_p, _u64p, ct.c_size_t], ct.c_int),
+    "ev_drop": ([_p, _u64p, ct.c_size_t], ct.c_int),
+    "ev_base": ([_p], ct.c_uint64),
+    "ev_backed": ([_p], ct.c_uint64),
+    "ev_reserved": ([_p], ct.c_uint64),
+    "ev_granularity": ([_p], ct.c_uint64),
+    "ev_poisoned": ([_p], ct.c_int),
+    "ev_close": ([_p], ct.c_int),
+    "ev_error": ([], ct.c_char_p),
+}
+
+EXPORTS = tuple(_KERNELS) + ("ekv_error", "ekv_abi_version") + tuple(_VMM)
+
+
+class KernelError(RuntimeError):
+    """A libekv_b200 entry point returned an error status."""
+
+
+@functools.lru_cache(maxsize=None)
+def library(path: str | None = None) -> ct.CDLL:
+    """Load and type the shared library (once per path)."""
+    path = path or os.environ.get("EKV_B200_LIBRARY") or str(LIBRARY_PATH)
+    try:
+        lib = ct.CDLL(path)
+    except OSError as exc:
+        raise RuntimeError(
+            f"libekv_b200.so could not be loaded from {path}; build it with "
+            "`python -m ekv_b200.build` (nvcc, sm_100a). There is no fallback path."
+        ) from exc
+    for name, argtypes in _KERNELS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = ct.c_int
+    lib.ekv_error.argtypes = []
+    lib.ekv_error.restype = ct.c_char_p
+    lib.ekv_abi_version.argtypes = []
+    lib.ekv_abi_version.restype = ct.c_int
+    for name, (argtypes, restype) in _VMM.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    return lib
+
+
+def call(name: str, *args) -> None:
+    """Invoke a kernel entry point; raise KernelError with its message on failure."""
+    lib = library()
+    if getattr(lib, name)(*args) != 0:
+        raise KernelError(f"{name}: {lib.ekv_error().decode('utf-8', 'replace')}")
+
+
+def u64_array(values) -> ct.Array:
+    values = [int(v) for v in values]
+    return (ct.c_uint64 * max(1, len(values)))(*values)
+
+
+def i64_array(values) -> ct.Array:
+    values = [int(v) for v in values]
+    return (ct.c_int64 * max(1, len(values)))(*values)
+
+
+def stream_handle(device: torch.device) -> int:
+    """Raw cudaStream_t of torch's current stream on `device` (0 = legacy default)."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_INDEX_SIZES = {torch.int32: 4, torch.int64: 8}
+
+
+def index_esize(tensor: torch.Tensor, name: str) -> int:
+    try:
+        return _INDEX_SIZES[tensor.dtype]
+    except KeyError:
+        raise TypeError(f"{name} must be an int32 or int64 tensor, got {tensor.dtype}") from None
+
+
+def require_cuda(tensors: dict, device: torch.device | None = None) -> torch.device:
+    """All named tensors must be CUDA tensors on one device; return it."""
+    for name, tensor in tensors.items():
+        if tensor is None:
+            continue
+        if not isinstance(tensor, torch.Tensor) or tensor.device.type != "cuda":
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if device is None:
+            device = tensor.device
+        elif tensor.device != device:
+            raise ValueError("all tensors must be on the same CUDA device")
+    if device is None:
+        raise ValueError("no CUDA tensor given")
+    return device
+
+
+def ptr(tensor: torch.Tensor | None) -> int | None:
+    return None if tensor is None else tensor.data_ptr()

@@ -1,0 +1,241 @@
+// Page -> chunk projection counts and the freeable-chunk bitmap (R4 / R6).
+//
+// A physical page of `page_size` token slots lives in every K/V plane; plane p
+// starts at chunk plane_chunk[p] and holds rows of plane_row_bytes[p] bytes, so
+// page g covers the byte range [g*page_size*row, (g+1)*page_size*row) of the
+// plane and the chunks under it (PhysicalPages.chunks,
+// adaptive_sparse/minimax_vmm.py:40-52).  A set of candidate pages frees chunk
+// c iff it holds every reference to c and c is mapped
+// (_releasable_counts, adaptive_sparse/scheduler_budget.py:159-162).
+//
+// chunk_counts is a histogram: tasks run plane-major so that the lanes of a
+// warp walk consecutive pages of one plane (usually the same chunk); lanes that
+// hit the same chunk are merged with __match_any_sync before one atomic, and
+// when the chunk table fits in shared memory each block accumulates a private
+// histogram there and flushes its non-zero bins once.  The bitmap is built with
+// warp ballots (32 chunks per ballot, two ballots per 64-bit word).
+#include "common.cuh"
+
+namespace ekv {
+namespace {
+
+struct CountParams {
+    const void* pages;
+    int32_t* counts;
+    int32_t* overflow;
+    int64_t n_pages, page_size, chunk_bytes, n_chunks;
+    int pages_es, n_planes;
+    int64_t plane_chunk[EKV_MAX_PLANES];
+    int64_t plane_row_bytes[EKV_MAX_PLANES];
+};
+
+constexpr int kCountThreads = 512;
+constexpr int64_t kSharedChunkLimit = 48 * 1024;  // 192 KiB of int32 bins
+
+// Add `amount` to bin `chunk`, merging lanes of the warp that target the same
+// bin.  All 32 lanes must call it (inactive lanes pass chunk = -1).
+template <bool kShared>
+__device__ __forceinline__ void add_bin(int32_t* bins, int64_t chunk, unsigned lane) {
+    const unsigned peers = __match_any_sync(0xffffffffu, static_cast<unsigned long long>(chunk));
+    const unsigned leader = __ffs(peers) - 1;
+    if (chunk >= 0 && lane == leader) {
+        atomicAdd(bins + chunk, __popc(peers));
+    }
+}
+
+template <bool kShared>
+__global__ void __launch_bounds__(kCountThreads)
+chunk_count_kernel(const __grid_constant__ CountParams p) {
+    extern __shared__ int32_t shared_bins[];
+    int32_t* bins = kShared ? shared_bins : p.counts;
+    if (kShared) {
+        for (int64_t c = threadIdx.x; c < p.n_chunks; c += kCountThreads) shared_bins[c] = 0;
+        __syncthreads();
+    }
+    const unsigned lane = lane_id();
+    const int64_t total = p.n_pages * p.n_planes;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kCountThreads;
+    // Round the loop bound up to a whole warp so every lane reaches the match.
+    const int64_t bound = (total + 31) & ~int64_t{31};
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kCountThreads + threadIdx.x; t < bound;
+         t += stride) {
+        int64_t first = -1, last = -2;
+        int64_t plane_base = 0;
+        if (t < total) {
+            const int64_t plane = t / p.n_pages;
+            const int64_t page = load_index(p.pages, p.pages_es, t - plane * p.n_pages);
+            const int64_t span = p.page_size * p.plane_row_bytes[plane];
+            const int64_t begin = page * span;
+            plane_base = p.plane_chunk[plane];
+            first = plane_base + begin / p.chunk_bytes;
+            last = plane_base + (begin + span - 1) / p.chunk_bytes;
+        }
+        // A page spans one chunk unless it crosses a boundary; walk the span
+        // in lock step so the match stays warp-wide.
+        int64_t steps = last - first + 1;
+        int64_t max_steps = steps;
+        for (int offset = 16; offset > 0; offset >>= 1) {
+            const int64_t other = __shfl_xor_sync(0xffffffffu, max_steps, offset);
+            max_steps = other > max_steps ? other : max_steps;
+        }
+        for (int64_t s = 0; s < max_steps; ++s) {
+            int64_t chunk = -1;
+            if (s < steps) {
+                chunk = first + s;
+                if (chunk < 0 || chunk >= p.n_chunks) {
+                    if (p.overflow) atomicAdd(p.overflow, 1);
+                    chunk = -1;
+                }
+            }
+            add_bin<kShared>(bins, chunk, lane);
+        }
+    }
+    if (kShared) {
+        __syncthreads();
+        for (int64_t c = threadIdx.x; c < p.n_chunks; c += kCountThreads) {
+            const int32_t v = shared_bins[c];
+            if (v) atomicAdd(p.counts + c, v);
+        }
+    }
+}
+
+constexpr int kBitmapThreads = 256;
+
+__global__ void __launch_bounds__(kBitmapThreads)
+freeable_kernel(const int32_t* __restrict__ counts, const int32_t* __restrict__ refs,
+                const uint64_t* __restrict__ mapped, int64_t n_chunks, uint64_t* __restrict__ out) {
+    const unsigned lane = lane_id();
+    const int64_t n_words = (n_chunks + 63) / 64;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (kBitmapThreads / 32);
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * (kBitmapThreads / 32) + (threadIdx.x >> 5);
+         w < n_words; w += warps) {
+        unsigned half[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int64_t c = w * 64 + h * 32 + lane;
+            bool freeable = false;
+            if (c < n_chunks) {
+                const int32_t count = counts[c];
+                freeable = count > 0 && count == refs[c];
+            }
+            half[h] = __ballot_sync(0xffffffffu, freeable);
+        }
+        if (lane == 0) {
+            out[w] = ((static_cast<uint64_t>(half[1]) << 32) | half[0]) & mapped[w];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kBitmapThreads)
+and_kernel(const uint64_t* __restrict__ gathered, int n_ranks, int64_t n_words,
+           uint64_t* __restrict__ out) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kBitmapThreads;
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * kBitmapThreads + threadIdx.x; w < n_words;
+         w += stride) {
+        uint64_t acc = ~uint64_t{0};
+        for (int r = 0; r < n_ranks; ++r) acc &= gathered[static_cast<int64_t>(r) * n_words + w];
+        out[w] = acc;
+    }
+}
+
+unsigned small_grid(int device, int64_t items, int per_block) {
+    const int64_t needed = (items + per_block - 1) / per_block;
+    const int64_t cap = static_cast<int64_t>(sm_count(device)) * 4;
+    return static_cast<unsigned>(needed < cap ? (needed > 0 ? needed : 1) : cap);
+}
+
+}  // namespace
+}  // namespace ekv
+
+using namespace ekv;
+
+extern "C" int ekv_chunk_counts(
+    const void* pages, int pages_esize, int64_t n_pages,
+    const int64_t* plane_chunk, const int64_t* plane_row_bytes, int n_planes,
+    int64_t page_size, int64_t chunk_bytes,
+    int32_t* counts, int64_t n_chunks, int accumulate, int32_t* overflow,
+    int device, void* stream) {
+    return guarded([&] {
+        require(n_pages >= 0 && n_chunks >= 0, "sizes must be non-negative");
+        require(page_size > 0 && chunk_bytes > 0, "page_size and chunk_bytes must be positive");
+        require(n_planes >= 1 && n_planes <= EKV_MAX_PLANES, "plane count outside [1, EKV_MAX_PLANES]");
+        require(plane_chunk && plane_row_bytes, "null plane table");
+        if (!n_chunks) return;
+        require(counts, "null counts");
+        bind_device(device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (!accumulate) {
+            cuda_check(cudaMemsetAsync(counts, 0, static_cast<size_t>(n_chunks) * sizeof(int32_t), s),
+                       "clear counts");
+        }
+        if (!n_pages) return;
+        require(pages, "null pages");
+        check_esize(pages_esize, "pages");
+        CountParams p{};
+        p.pages = pages;
+        p.counts = counts;
+        p.overflow = overflow;
+        p.n_pages = n_pages;
+        p.page_size = page_size;
+        p.chunk_bytes = chunk_bytes;
+        p.n_chunks = n_chunks;
+        p.pages_es = pages_esize;
+        p.n_planes = n_planes;
+        for (int i = 0; i < n_planes; ++i) {
+            require(plane_row_bytes[i] > 0 && plane_chunk[i] >= 0, "invalid plane geometry");
+            p.plane_chunk[i] = plane_chunk[i];
+            p.plane_row_bytes[i] = plane_row_bytes[i];
+        }
+        const int64_t tasks = n_pages * n_planes;
+        if (n_chunks <= kSharedChunkLimit) {
+            const size_t smem = static_cast<size_t>(n_chunks) * sizeof(int32_t);
+            static bool configured[64] = {false};
+            if (device < 64 && !configured[device]) {
+                cuda_check(cudaFuncSetAttribute(chunk_count_kernel<true>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(kSharedChunkLimit * sizeof(int32_t))),
+                           "configure shared histogram");
+                configured[device] = true;
+            }
+            // Few blocks: each one pays a full-table flush.
+            const int64_t needed = (tasks + kCountThreads - 1) / kCountThreads;
+            const int64_t cap = sm_count(device);
+            const unsigned grid = static_cast<unsigned>(needed < cap ? needed : cap);
+            chunk_count_kernel<true><<<grid, kCountThreads, smem, s>>>(p);
+        } else {
+            const unsigned grid = small_grid(device, tasks, kCountThreads);
+            chunk_count_kernel<false><<<grid, kCountThreads, 0, s>>>(p);
+        }
+        check_launch("chunk_counts launch");
+    });
+}
+
+extern "C" int ekv_freeable_bitmap(
+    const int32_t* counts, const int32_t* refs, const uint64_t* mapped_bits,
+    int64_t n_chunks, uint64_t* out_bits, int device, void* stream) {
+    return guarded([&] {
+        require(n_chunks >= 0, "n_chunks must be non-negative");
+        if (!n_chunks) return;
+        require(counts && refs && mapped_bits && out_bits, "null pointer argument");
+        bind_device(device);
+        const int64_t words = (n_chunks + 63) / 64;
+        freeable_kernel<<<small_grid(device, words, kBitmapThreads / 32), kBitmapThreads, 0,
+                          static_cast<cudaStream_t>(stream)>>>(counts, refs, mapped_bits, n_chunks,
+                                                               out_bits);
+        check_launch("freeable_bitmap launch");
+    });
+}
+
+extern "C" int ekv_bitmap_and(
+    const uint64_t* gathered, int n_ranks, int64_t n_words, uint64_t* out,
+    int device, void* stream) {
+    return guarded([&] {
+        require(n_ranks >= 1 && n_words >= 0, "need at least one rank and non-negative words");
+        if (!n_words) return;
+        require(gathered && out, "null pointer argument");
+        bind_device(device);
+        and_kernel<<<small_grid(device, n_words, kBitmapThreads), kBitmapThreads, 0,
+                     static_cast<cudaStream_t>(stream)>>>(gathered, n_ranks, n_words, out);
+        check_launch("bitmap_and launch");
+    });
+}

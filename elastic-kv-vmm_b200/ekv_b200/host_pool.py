@@ -1,0 +1,184 @@
+"""Demote/promote data movement (R5): row pack/unpack and a pinned host KV pool.
+
+The reference's migration transactions (adaptive_sparse/migration.py) move
+rows through SGLang's host KV pool: ``alloc_paged_token_slots``,
+``backup_from_device_all_layer`` (migration.py:105-111), ``load_to_device_per_layer``
+(migration.py:231-234), ``allocated_host_indices`` and ``free``
+(migration.py:58-63).  ``PinnedHostKVPool`` implements exactly those methods
+on top of the pack/unpack kernels, so ``migration.py`` drives it unchanged.
+
+Host layout: plane-major ("layer first"): plane p (K of layer l at p = 2l,
+V at p = 2l + 1) is a region of ``capacity`` rows starting on a 2 MiB
+boundary, so a device chunk's worth of rows maps onto a chunk-aligned host
+range.  The pinned buffer is addressed by the kernels directly through
+unified addressing; rows cross the host link as the kernel's 16-byte stores
+(demote) or loads (promote).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import MAX_PLANES, call, index_esize, require_cuda, stream_handle, u64_array
+
+CHUNK_BYTES = 2 << 20
+
+
+def _plane_rows(planes):
+    planes = list(planes)
+    if not planes:
+        raise ValueError("need at least one plane")
+    row_bytes = planes[0][0].numel() * planes[0].element_size()
+    for plane in planes:
+        if not plane.is_contiguous():
+            raise ValueError("planes must be contiguous")
+        if plane[0].numel() * plane.element_size() != row_bytes:
+            raise ValueError("all planes must share one row size")
+    return planes, row_bytes
+
+
+def _row_copy(kind, planes, slots, staging, *, plane_index=None, stage_rows=None,
+              stage_plane_stride=0, device=None, stream=None):
+    planes, row_bytes = _plane_rows(planes)
+    if len(planes) > MAX_PLANES:
+        raise ValueError("more planes than EKV_MAX_PLANES in one call")
+    device = require_cuda(dict(slots=slots, plane_index=plane_index, stage_rows=stage_rows,
+                               **{f"plane{i}": p for i, p in enumerate(planes)}), device)
+    if not slots.is_contiguous() or slots.dim() != 1:
+        raise ValueError("slots must be a contiguous 1-D tensor")
+    if plane_index is not None:
+        if plane_index.dtype != torch.int32 or plane_index.numel() != slots.numel():
+            raise ValueError("plane_index must be int32 with one entry per slot")
+        n_tasks = slots.numel()
+    else:
+        n_tasks = len(planes) * slots.numel()
+    if stage_rows is not None and stage_rows.numel() != slots.numel():
+        raise ValueError("stage_rows must have one entry per slot")
+    if not staging.is_contiguous():
+        raise ValueError("staging must be contiguous")
+    if staging.device.type == "cpu" and not staging.is_pinned():
+        raise ValueError("host staging must be pinned memory")
+    call(
+        kind,
+        u64_array(p.data_ptr() for p in planes), len(planes), row_bytes,
+        None if plane_index is None else plane_index.data_ptr(),
+        slots.data_ptr(), index_esize(slots, "slots"), slots.numel(),
+        None if stage_rows is None else stage_rows.data_ptr(),
+        8 if stage_rows is None else index_esize(stage_rows, "stage_rows"),
+        staging.data_ptr(), int(stage_plane_stride), n_tasks,
+        device.index, stream if stream is not None else stream_handle(device),
+    )
+
+
+def pack_rows(planes, slots, staging, **kwargs):
+    """Copy rows ``planes[p][slots[j]]`` into ``staging`` (device or pinned host).
+
+    Cross form (``plane_index`` None): plane p's row j lands at byte
+    ``p * stage_plane_stride + (stage_rows[j] if given else j) * row_bytes``.
+    List form: task t copies ``planes[plane_index[t]][slots[t]]`` to row
+    ``stage_rows[t]`` (or t) of ``staging``.
+    """
+    _row_copy("ekv_pack_rows", planes, slots, staging, **kwargs)
+
+
+def unpack_rows(planes, slots, staging, **kwargs):
+    """Inverse of ``pack_rows``: staging rows back into ``planes`` at ``slots``."""
+    _row_copy("ekv_unpack_rows", planes, slots, staging, **kwargs)
+
+
+def pinned_buffer(nbytes: int) -> torch.Tensor:
+    """Pinned host bytes, rounded up to whole 2 MiB chunks."""
+    rounded = -(-nbytes // CHUNK_BYTES) * CHUNK_BYTES
+    return torch.empty(rounded, dtype=torch.uint8, pin_memory=True)
+
+
+class PinnedHostKVPool:
+    """Host KV pool with SGLang HostKVCache's migration methods.
+
+    ``capacity`` token rows per plane, ``layer_num`` layers of K and V, rows of
+    ``row_bytes`` bytes.  Host slots are handed out one token at a time (page
+    size 1 on the host; device page structure is preserved by the indices the
+    caller passes).
+    """
+
+    def __init__(self, capacity: int, layer_num: int, row_bytes: int, device, dtype=torch.bfloat16):
+        self.capacity = int(capacity)
+        self.layer_num = int(layer_num)
+        self.row_bytes = int(row_bytes)
+        self.device = torch.device(device)
+        self.dtype = dtype
+        plane_bytes = self.capacity * self.row_bytes
+        self.plane_stride = -(-plane_bytes // CHUNK_BYTES) * CHUNK_BYTES
+        self.buffer = pinned_buffer(self.plane_stride * 2 * self.layer_num)
+        self._free = torch.ones(self.capacity, dtype=torch.bool)
+
+    # --- allocation (host indices are int64 row numbers) ---------------------
+
+    def available_size(self) -> int:
+        return int(self._free.sum())
+
+    def alloc(self, need: int) -> torch.Tensor | None:
+        free = torch.nonzero(self._free).flatten()
+        if free.numel() < need:
+            return None
+        chosen = free[:need]
+        self._free[chosen] = False
+        return chosen
+
+    def free(self, indices: torch.Tensor) -> int:
+        indices = indices.to("cpu", torch.int64)
+        if (~self._free[indices]).sum() != indices.numel():
+            raise RuntimeError("double free of host KV rows")
+        self._free[indices] = True
+        return indices.numel()
+
+    def alloc_paged_token_slots(self, req_to_host_pool, allocated_len, row, start, length):
+        """Allocate host rows for tokens [start, length) of request row ``row``."""
+        need = length - start
+        indices = self.alloc(need)
+        if indices is None:
+            raise MemoryError("host KV pool exhausted")
+        req_to_host_pool[row, start:length] = indices.to(req_to_host_pool.device, req_to_host_pool.dtype)
+        allocated_len[row] = length
+        return req_to_host_pool[row, :length]
+
+    def allocated_host_indices(self, req_to_host_pool, row, length):
+        return req_to_host_pool[row, :int(length)]
+
+    # --- data movement --------------------------------------------------------
+
+    def plane_view(self, plane: int) -> torch.Tensor:
+        """Host rows of plane ``plane`` as [capacity, row_bytes] uint8."""
+        start = plane * self.plane_stride
+        return self.buffer[start:start + self.capacity * self.row_bytes].view(self.capacity, self.row_bytes)
+
+    @staticmethod
+    def _device_planes(device_pool, layers):
+        planes = []
+        for layer in layers:
+            planes.append(device_pool.get_key_buffer(layer))
+            planes.append(device_pool.get_value_buffer(layer))
+        return planes
+
+    def backup_from_device_all_layer(self, device_pool, host_indices, device_indices,
+                                     io_backend="kernel"):
+        """Copy rows ``device_indices`` of every layer's K and V to host rows ``host_indices``."""
+        layers = range(getattr(device_pool, "start_layer", 0),
+                       getattr(device_pool, "end_layer", self.layer_num))
+        planes = self._device_planes(device_pool, layers)
+        slots = device_indices.to(self.device, torch.int64).contiguous()
+        rows = host_indices.to(self.device, torch.int64).contiguous()
+        base = self.buffer[layers.start * 2 * self.plane_stride:]
+        for start in range(0, len(planes), MAX_PLANES):
+            chunk = planes[start:start + MAX_PLANES]
+            pack_rows(chunk, slots, base[start * self.plane_stride:], stage_rows=rows,
+                      stage_plane_stride=self.plane_stride)
+
+    def load_to_device_per_layer(self, device_pool, host_indices, device_indices, layer_id,
+                                 io_backend="kernel"):
+        """Copy host rows ``host_indices`` of layer ``layer_id`` into K/V rows ``device_indices``."""
+        planes = self._device_planes(device_pool, [layer_id])
+        slots = device_indices.to(self.device, torch.int64).contiguous()
+        rows = host_indices.to(self.device, torch.int64).contiguous()
+        base = self.buffer[2 * layer_id * self.plane_stride:]
+        unpack_rows(planes, slots, base, stage_rows=rows, stage_plane_stride=self.plane_stride)

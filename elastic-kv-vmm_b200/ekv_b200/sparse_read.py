@@ -1,0 +1,163 @@
+"""Top-K K/V row gather on sm_100a (R3).
+
+``gather_rows`` keeps the signature, checks and zero-fill of the reference's
+experimental/sparse_read.py:33-51.  ``gather_rows_planes`` applies one row
+selection to many planes (every layer's K and V) in a single launch, resolving
+the index chain once per row; it is the form the decode path and the benchmark
+use.
+"""
+
+from __future__ import annotations
+
+from ._lib import MAX_PLANES, call, index_esize, require_cuda, stream_handle, u64_array
+
+
+def _index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect):
+    if indirect and (request_table is None or slot_offsets is None):
+        raise ValueError("indirect gather needs request_table and slot_offsets")
+    table = request_table if indirect else None
+    offsets = slot_offsets if indirect else None
+    return (
+        positions.data_ptr(), index_esize(positions, "positions"),
+        request_ids.data_ptr(), index_esize(request_ids, "request_ids"),
+        lengths.data_ptr(), index_esize(lengths, "lengths"),
+        None if table is None else table.data_ptr(),
+        8 if table is None else index_esize(table, "request_table"),
+        None if offsets is None else offsets.data_ptr(),
+        8 if offsets is None else index_esize(offsets, "slot_offsets"),
+    )
+
+
+def _check_contiguous(tensors):
+    for name, tensor in tensors.items():
+        if tensor is not None and not tensor.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+
+
+def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offsets,
+                output, layout, *, indirect):
+    """All tensors must be contiguous CUDA tensors on the same device.
+
+    ``output[b, i, :]`` is the ``layout.row_elements``-element row of ``raw``
+    at element offset ``slot_offsets[request_table[request_ids[b], pos]]``
+    (indirect) or ``sink + request_ids[b] * request_stride + pos * width``
+    (direct, strides from ``layout``), with ``pos = positions[b, i]``; rows
+    with ``pos`` outside ``[0, lengths[b])`` are zero.  Table values are
+    ELEMENT offsets into ``raw``.  ``raw`` and ``output`` share a dtype: the
+    payload is copied bit for bit.
+    """
+    batch, selected = positions.shape
+    if output.shape != (batch, selected, layout.row_elements):
+        raise ValueError("output shape does not match positions and row width")
+    if not batch or not selected:
+        return
+    tensors = dict(raw=raw, positions=positions, request_ids=request_ids, lengths=lengths,
+                   request_table=request_table, slot_offsets=slot_offsets, output=output)
+    device = require_cuda(tensors)
+    _check_contiguous(tensors)
+    if raw.dtype != output.dtype:
+        raise TypeError("raw and output must have the same dtype (bitwise row copy)")
+    call(
+        "ekv_gather_rows",
+        raw.data_ptr(), output.data_ptr(), raw.element_size(),
+        *_index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect),
+        batch, selected, layout.row_elements,
+        layout.max_tokens, layout.request_bytes // layout.itemsize,
+        layout.chunk_bytes // layout.itemsize,
+        int(bool(indirect)), device.index, stream_handle(device),
+    )
+
+
+def gather_rows_planes(planes, positions, request_ids, lengths, request_table, slot_offsets,
+                       outputs, layout, *, indirect):
+    """``gather_rows`` over every plane in ``planes`` with one row selection.
+
+    ``planes[p]`` and ``outputs[p]`` play the roles of ``raw`` and ``output``
+    for plane p (e.g. layer l's K at p = 2l and V at p = 2l + 1).  Element
+    offsets are relative to each plane's start.  Planes are processed
+    EKV_MAX_PLANES per launch.
+    """
+    planes = list(planes)
+    outputs = list(outputs)
+    if len(planes) != len(outputs):
+        raise ValueError("planes and outputs differ in length")
+    batch, selected = positions.shape
+    for output in outputs:
+        if output.shape != (batch, selected, layout.row_elements):
+            raise ValueError("output shape does not match positions and row width")
+    if not planes or not batch or not selected:
+        return
+    index = dict(positions=positions, request_ids=request_ids, lengths=lengths,
+                 request_table=request_table, slot_offsets=slot_offsets)
+    device = require_cuda(index)
+    _check_contiguous(index)
+    itemsize = planes[0].element_size()
+    for plane, output in zip(planes, outputs):
+        require_cuda(dict(plane=plane, output=output), device)
+        if not plane.is_contiguous() or not output.is_contiguous():
+            raise ValueError("planes and outputs must be contiguous")
+        if plane.dtype != output.dtype or plane.element_size() != itemsize:
+            raise TypeError("all planes and outputs must share one dtype")
+    args = _index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect)
+    stream = stream_handle(device)
+    for start in range(0, len(planes), MAX_PLANES):
+        src = planes[start:start + MAX_PLANES]
+        dst = outputs[start:start + MAX_PLANES]
+        call(
+            "ekv_gather_rows_planes",
+            u64_array(t.data_ptr() for t in src), u64_array(t.data_ptr() for t in dst), len(src),
+            itemsize, *args, batch, selected, layout.row_elements,
+            layout.max_tokens, layout.request_bytes // layout.itemsize,
+            layout.chunk_bytes // layout.itemsize,
+            int(bool(indirect)), device.index, stream,
+        )
+
+
+class PlaneGather:
+    """Pre-bound plane gather for a hot loop: plane/output pointer tables and
+    the index tensors are fixed at construction, so each call only launches.
+
+    The tensors passed here must outlive the object and keep their storage.
+    """
+
+    def __init__(self, planes, positions, request_ids, lengths, request_table, slot_offsets,
+                 outputs, layout, *, indirect):
+        planes = list(planes)
+        outputs = list(outputs)
+        if not planes or len(planes) != len(outputs) or len(planes) > MAX_PLANES:
+            raise ValueError("need 1..EKV_MAX_PLANES planes with one output each")
+        batch, selected = positions.shape
+        for output in outputs:
+            if output.shape != (batch, selected, layout.row_elements):
+                raise ValueError("output shape does not match positions and row width")
+        index = dict(positions=positions, request_ids=request_ids, lengths=lengths,
+                     request_table=request_table, slot_offsets=slot_offsets)
+        self.device = require_cuda(index)
+        _check_contiguous(index)
+        for plane, output in zip(planes, outputs):
+            require_cuda(dict(plane=plane, output=output), self.device)
+            if not plane.is_contiguous() or not output.is_contiguous():
+                raise ValueError("planes and outputs must be contiguous")
+            if plane.dtype != output.dtype or plane.dtype != planes[0].dtype:
+                raise TypeError("all planes and outputs must share one dtype")
+        self._keep = (planes, outputs, index)
+        self._src = u64_array(t.data_ptr() for t in planes)
+        self._dst = u64_array(t.data_ptr() for t in outputs)
+        self._args = (
+            self._src, self._dst, len(planes), planes[0].element_size(),
+            *_index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect),
+            batch, selected, layout.row_elements,
+            layout.max_tokens, layout.request_bytes // layout.itemsize,
+            layout.chunk_bytes // layout.itemsize, int(bool(indirect)), self.device.index,
+        )
+        self.empty = not batch or not selected
+
+    def __call__(self, stream: int | None = None) -> None:
+        if self.empty:
+            return
+        if stream is None:
+            stream = stream_handle(self.device)
+        call("ekv_gather_rows_planes", *self._args, stream)
+
+
+__all__ = ["gather_rows", "gather_rows_planes", "PlaneGather"]

@@ -1,0 +1,201 @@
+/*
+ * ekv_kernels.h — C ABI of libekv_b200.so, the sm_100a data path for sparse-KV
+ * residency: lookup, Top-K row gather, demote/promote row migration and the
+ * per-chunk freeable bitmap with its cross-rank AND.
+ *
+ * Conventions (same as the reference's ev_* ABI, native/elastic_vmm.cpp:289-369):
+ *   - every function returns int: 0 on success, -1 on error;
+ *   - ekv_error() returns the calling thread's last error message ("" if none);
+ *   - pointers are plain device addresses (or mapped pinned-host addresses where
+ *     a parameter says so); strides and sizes are int64 element counts unless a
+ *     name ends in _bytes;
+ *   - index arrays carry their element size (4 = int32, 8 = int64) in the
+ *     matching *_esize argument; values are read as signed integers;
+ *   - `device` is the CUDA ordinal that owns `stream` and every buffer; the call
+ *     makes it current for the calling thread before launching;
+ *   - work is launched asynchronously on `stream` (a cudaStream_t, NULL = the
+ *     legacy default stream); no call synchronizes, allocates device memory, or
+ *     retains a pointer after it returns.
+ * Threading: calls may come from any thread; concurrent calls that write the
+ * same buffers race exactly as two kernels on different streams would.
+ */
+#ifndef EKV_KERNELS_H
+#define EKV_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Largest number of planes (K/V tensors of individual layers) one call takes. */
+#define EKV_MAX_PLANES 256
+
+/* Thread-local message of the last failed call on this thread. */
+const char* ekv_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+int ekv_abi_version(void);
+
+/*
+ * R1 — resident lookup.  Replaces the Triton `_resolve` launch of
+ * resolve_resident (adaptive_sparse/resident_lookup.py:6-40).
+ * For every s < n_selected, row = selected[s], and every column j < width
+ * (width = topk_width * block_size):
+ *     block = topk[row, j / block_size];  pos = block * block_size + j % block_size
+ *     out[row, j] = (block >= 0 && pos < lengths[row])
+ *                   ? (int32) mapping[table[rows[row], pos]] : -1
+ * Rows not listed in `selected` are not written.  All arrays are strided.
+ */
+int ekv_resolve_resident(
+    const void* topk, int topk_esize, int64_t topk_row_stride, int64_t topk_col_stride,
+    int64_t topk_width,
+    const void* table, int table_esize, int64_t table_row_stride, int64_t table_col_stride,
+    const void* mapping, int mapping_esize, int64_t mapping_stride,
+    const void* rows, int rows_esize, int64_t rows_stride,
+    const void* lengths, int lengths_esize, int64_t lengths_stride,
+    const void* selected, int selected_esize, int64_t selected_stride, int64_t n_selected,
+    int32_t* out, int64_t out_row_stride, int64_t out_col_stride,
+    int64_t block_size, int device, void* stream);
+
+/*
+ * R2 — logical-token -> hot-slot lookup with miss detection and compaction.
+ * No single reference symbol: R1 with `mapping` replaced by a per-request
+ * residency map (-1 = not resident), plus the hit/miss contract of the swap
+ * kernel exercised by tests/smoke_minimax_swap.py:28-62.
+ * For b < batch, i < k:  t = topk[b, i]; n = min(lengths[b], map_width)
+ *     valid = 0 <= t < n;  slot = valid ? res_map[b, t] : -1
+ *     slots[b, i] = slot;  miss[b, i] = valid && slot < 0
+ * miss_list[b, :] holds the token ids t of row b's misses in ascending i order,
+ * followed by -1 up to k; miss_count[b] is their number.  lengths may be NULL
+ * (n = map_width); miss, miss_list and miss_count may each be NULL.
+ */
+int ekv_lookup_slots(
+    const void* res_map, int map_esize, int64_t map_row_stride, int64_t map_width,
+    const void* topk, int topk_esize, int64_t topk_row_stride,
+    const void* lengths, int lengths_esize,
+    int64_t batch, int64_t k,
+    int32_t* slots, int64_t slots_row_stride,
+    uint8_t* miss, int64_t miss_row_stride,
+    int32_t* miss_list, int64_t miss_list_row_stride,
+    int32_t* miss_count,
+    int device, void* stream);
+
+/*
+ * R3 — Top-K row gather.  Replaces the Triton `_gather` launch of gather_rows
+ * (experimental/sparse_read.py:11-51).  For b < batch, i < selected:
+ *     pos = positions[b*selected + i], req = request_ids[b]
+ *     valid = 0 <= pos < lengths[b]
+ *     off = indirect ? slot_offsets[request_table[req*table_width + pos]]
+ *                    : sink_elements + req*request_stride + pos*width
+ *     out[(b*selected + i)*width + c] = valid ? raw[off + c] : 0,  c < width
+ * Offsets, strides and width are counted in elements of `itemsize` bytes; the
+ * payload is copied bit for bit.  Index arrays are contiguous.
+ */
+int ekv_gather_rows(
+    const void* raw, void* out, int64_t itemsize,
+    const void* positions, int positions_esize,
+    const void* request_ids, int request_ids_esize,
+    const void* lengths, int lengths_esize,
+    const void* request_table, int table_esize,
+    const void* slot_offsets, int offsets_esize,
+    int64_t batch, int64_t selected, int64_t width,
+    int64_t table_width, int64_t request_stride, int64_t sink_elements,
+    int indirect, int device, void* stream);
+
+/*
+ * R3, batched over planes — the same row selection applied to n_planes
+ * source planes at once (all layers' K and V in one launch; the index chain is
+ * resolved once per row).  src_planes / dst_planes are HOST arrays of n_planes
+ * device addresses (n_planes <= EKV_MAX_PLANES); plane p's row comes from
+ * src_planes[p] + off*itemsize and lands at dst_planes[p] + (b*selected+i)*width*itemsize.
+ */
+int ekv_gather_rows_planes(
+    const uint64_t* src_planes, const uint64_t* dst_planes, int n_planes, int64_t itemsize,
+    const void* positions, int positions_esize,
+    const void* request_ids, int request_ids_esize,
+    const void* lengths, int lengths_esize,
+    const void* request_table, int table_esize,
+    const void* slot_offsets, int offsets_esize,
+    int64_t batch, int64_t selected, int64_t width,
+    int64_t table_width, int64_t request_stride, int64_t sink_elements,
+    int indirect, int device, void* stream);
+
+/*
+ * R5 — migration row copies between KV planes and a staging buffer.  Replaces
+ * the data movement of HostKVCache.backup_from_device_all_layer /
+ * load_to_device_per_layer called at adaptive_sparse/migration.py:109-111 and
+ * :231-237.  `staging` may be device memory or pinned host memory that is
+ * mapped into the device address space (cudaHostAlloc / cudaHostRegister).
+ *
+ * Task list: n_tasks rows.  Task t copies row_bytes between
+ *     plane  planes[p] + slot*row_bytes   and   staging + soff
+ * where
+ *   plane_index != NULL ("list" form):
+ *       p = plane_index[t] (int32), slot = slots[t], soff = stage_rows ? stage_rows[t]*row_bytes
+ *                                                                       : t*row_bytes
+ *   plane_index == NULL ("cross" form, n_tasks = n_planes * n_slots):
+ *       p = t / n_slots, j = t % n_slots, slot = slots[j],
+ *       soff = p*stage_plane_stride_bytes + (stage_rows ? stage_rows[j] : j)*row_bytes
+ * ekv_pack_rows copies plane -> staging, ekv_unpack_rows staging -> plane.
+ * planes is a HOST array of n_planes device addresses.
+ */
+int ekv_pack_rows(
+    const uint64_t* planes, int n_planes, int64_t row_bytes,
+    const int32_t* plane_index, const void* slots, int slots_esize, int64_t n_slots,
+    const void* stage_rows, int stage_rows_esize,
+    void* staging, int64_t stage_plane_stride_bytes, int64_t n_tasks,
+    int device, void* stream);
+
+int ekv_unpack_rows(
+    const uint64_t* planes, int n_planes, int64_t row_bytes,
+    const int32_t* plane_index, const void* slots, int slots_esize, int64_t n_slots,
+    const void* stage_rows, int stage_rows_esize,
+    const void* staging, int64_t stage_plane_stride_bytes, int64_t n_tasks,
+    int device, void* stream);
+
+/*
+ * R4/R6 — page -> chunk projection counts.  Restates PhysicalPages.chunks
+ * (adaptive_sparse/minimax_vmm.py:40-52) and _chunk_release_counts
+ * (adaptive_sparse/scheduler_budget.py:155-156): for each page and plane p,
+ * the chunks plane_chunk[p] + [page*page_size*row_bytes[p] / chunk_bytes,
+ * (page*page_size*row_bytes[p] + page_size*row_bytes[p] - 1) / chunk_bytes]
+ * each get +1 in counts[0:n_chunks] (int32).  Pages must be distinct.  When
+ * `accumulate` is 0 counts is cleared first.  plane_chunk / plane_row_bytes are
+ * HOST arrays of n_planes values.  Chunks >= n_chunks are counted in
+ * *overflow (device int32, may be NULL) instead of being written.
+ */
+int ekv_chunk_counts(
+    const void* pages, int pages_esize, int64_t n_pages,
+    const int64_t* plane_chunk, const int64_t* plane_row_bytes, int n_planes,
+    int64_t page_size, int64_t chunk_bytes,
+    int32_t* counts, int64_t n_chunks, int accumulate, int32_t* overflow,
+    int device, void* stream);
+
+/*
+ * R6 — freeable bitmap.  Restates _releasable_counts
+ * (adaptive_sparse/scheduler_budget.py:159-162): bit c of out_bits is set iff
+ *     counts[c] > 0 && counts[c] == refs[c] && bit c of mapped_bits is set.
+ * Bitmaps are uint64 words, chunk c at word c/64, bit c%64; bits >= n_chunks
+ * of the last word are 0.
+ */
+int ekv_freeable_bitmap(
+    const int32_t* counts, const int32_t* refs, const uint64_t* mapped_bits,
+    int64_t n_chunks, uint64_t* out_bits, int device, void* stream);
+
+/*
+ * R6 — cross-rank combine: out[w] = AND over r < n_ranks of gathered[r*n_words + w].
+ * Replaces the candidate-key intersection of rank_demotions
+ * (adaptive_sparse/runtime_value.py:180-185) over the exchange() of
+ * adaptive_sparse/scheduler_budget.py:1447-1452 for the joint chunk set;
+ * `gathered` is the NCCL all-gather of every rank's bitmap.
+ */
+int ekv_bitmap_and(
+    const uint64_t* gathered, int n_ranks, int64_t n_words, uint64_t* out,
+    int device, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EKV_KERNELS_H */

@@ -1,0 +1,51 @@
+"""Timed CPU baseline of the data path -- test / benchmark infrastructure only.
+
+Multi-threaded torch-CPU restatements of the reference's CPU-capable path,
+run on the host cores for the ``cpu_baseline`` leg and the ``--impl reference``
+arm of bench.py:
+
+* gather: the row selection of experimental/sparse_read.py:18-30 (indirect:
+  positions -> request_table -> slot_offsets; invalid rows zero) as
+  ``index_select`` over every plane;
+* lookup: the reference's own torch resolver expression
+  (adaptive_sparse/request_residency.py:819-826) on CPU tensors.
+
+The reference has no CPU implementation of its Triton gather; this
+restatement is the "port" baseline and is checked against the numpy oracle
+in tests.
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+def gather_planes(planes, positions, request_ids, lengths, request_table, slot_offsets, width, outputs):
+    """``outputs[p][b, i] = planes[p][slot_offsets[table[req, pos]] // width]`` or 0.
+
+    ``planes[p]`` is [slots, width] (any dtype), ``outputs[p]`` [B, S, width].
+    Offsets must be whole rows (multiples of ``width``), as in the benchmark layout.
+    """
+    pos = positions.to(torch.int64)
+    valid = (pos >= 0) & (pos < lengths.to(torch.int64)[:, None])
+    safe = torch.where(valid, pos, torch.zeros_like(pos))
+    logical = request_table[request_ids.to(torch.int64)[:, None], safe]
+    rows = torch.div(slot_offsets[logical], width, rounding_mode="floor")
+    rows = torch.where(valid, rows, torch.zeros_like(rows)).reshape(-1)
+    invalid = ~valid.reshape(-1)
+    any_invalid = bool(invalid.any())
+    for plane, out in zip(planes, outputs):
+        flat = out.view(-1, width)
+        torch.index_select(plane, 0, rows, out=flat)
+        if any_invalid:
+            flat[invalid] = 0
+
+
+def torch_resolver(topk, table, mapping, rows, lengths, selected, result, block_size):
+    """The reference's torch resolver (request_residency.py:819-826) on any device."""
+    blocks = topk[0, selected].long()
+    positions = blocks.unsqueeze(-1) * block_size + torch.arange(block_size, device=rows.device)
+    positions = positions.flatten(1)
+    valid = (positions >= 0) & (positions < lengths[selected, None])
+    logical = table[rows[selected, None], positions.masked_fill(~valid, 0)]
+    result[0, selected] = mapping[logical].masked_fill(~valid, -1).to(torch.int32)

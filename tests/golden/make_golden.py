@@ -1,0 +1,257 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE code.
+
+Run in a container where the reference checkout is importable:
+
+    EKV_REFERENCE=/path/to/elastic-kv-vmm TRITON_INTERPRET=1 python tests/golden/make_golden.py
+
+The reference's Triton kernels (adaptive_sparse/resident_lookup.py,
+experimental/sparse_read.py) run on CPU tensors under the Triton interpreter;
+its Python helpers (VirtualKVLayout, PhysicalPages.chunks, _releasable*,
+plan_demote_pages) run as they are.  Inputs are seeded; every fixture stores
+inputs and the reference's outputs.  The captured TP4 plan state
+results/vmm-pair12k-shadow/adaptive_stats/plans-rank0{0..3}.json is reduced to
+the fields the freeable-bitmap test needs.  Nothing in the test suite reads
+the reference at run time: only these files.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import random
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REFERENCE = Path(os.environ.get("EKV_REFERENCE", "/root/reference"))
+
+
+def _import_reference():
+    if os.environ.get("TRITON_INTERPRET") != "1":
+        raise SystemExit("set TRITON_INTERPRET=1 so the reference Triton kernels run on CPU")
+    sys.path.insert(0, str(REFERENCE))
+    import torch  # noqa: F401
+
+    from adaptive_sparse import minimax_vmm, migration, scheduler_budget
+    from adaptive_sparse.resident_lookup import resolve_resident
+    from experimental.sparse_read import gather_rows
+    from experimental.virtual_layout import VirtualKVLayout
+
+    return dict(resolve_resident=resolve_resident, gather_rows=gather_rows,
+                VirtualKVLayout=VirtualKVLayout, PhysicalPages=minimax_vmm.PhysicalPages,
+                scheduler_budget=scheduler_budget, migration=migration)
+
+
+def lookup_cases(ref):
+    import torch
+
+    cases = {}
+
+    def run(name, topk, table, mapping, rows, lengths, selected, width_out, block_size, init=-77):
+        out = torch.full((1, topk.shape[1], width_out), init, dtype=torch.int32)
+        ref["resolve_resident"](topk, table, mapping, rows, lengths, selected, out, block_size)
+        cases[name] = dict(topk=topk.numpy(), table=table.numpy(), mapping=mapping.numpy(),
+                           rows=rows.numpy(), lengths=lengths.numpy(), selected=selected.numpy(),
+                           block_size=np.int64(block_size), init=np.int32(init), expected=out.numpy())
+
+    # The vectors of tests/smoke_resident_lookup.py:8-13.
+    run("smoke",
+        torch.tensor([[[1, -1, 2] + [-1] * 13, [0] * 16, [0, 2, -1] + [-1] * 13]], dtype=torch.int32),
+        torch.tensor([[i * 300 + j for j in range(300)] for i in range(4)], dtype=torch.int64),
+        torch.tensor([i * 3 + 5 for i in range(1200)], dtype=torch.int64),
+        torch.tensor([3, 0, 1], dtype=torch.int64), torch.tensor([130, 0, 0], dtype=torch.int32),
+        torch.tensor([2, 0], dtype=torch.int64), 2048, 128)
+
+    gen = torch.Generator().manual_seed(20261201)
+    for name, (batch, k, bs, width, tdtype, mdtype) in {
+        "random_bs4": (6, 7, 4, 40, torch.int32, torch.int64),
+        "random_bs1": (9, 300, 1, 512, torch.int64, torch.int32),
+        "random_bs16_big": (4, 40, 16, 1024, torch.int32, torch.int64),
+    }.items():
+        reqs = batch + 3
+        table = torch.randint(0, 5000, (reqs, width), generator=gen).to(tdtype)
+        mapping = (torch.randint(-(1 << 33), 1 << 33, (5000,), generator=gen)
+                   if mdtype == torch.int64 else torch.randint(-9, 1 << 20, (5000,), generator=gen)).to(mdtype)
+        n_blocks = width // bs
+        topk = torch.randint(-1, n_blocks + 2, (1, batch, k), generator=gen).to(torch.int32)
+        lengths = torch.randint(0, width + 1, (batch,), generator=gen).to(torch.int32)
+        rows = torch.randint(0, reqs, (batch,), generator=gen).to(torch.int64)
+        selected = torch.randperm(batch, generator=gen)[: max(1, batch - 2)].to(torch.int64)
+        run(name, topk, table, mapping, rows, lengths, selected, k * bs, bs)
+    return cases
+
+
+def gather_cases(ref):
+    import torch
+
+    cases = {}
+    gen = torch.Generator().manual_seed(97)
+    for name, (reqs, tokens, width, chunk, batch, selected) in {
+        "small_w24": (3, 37, 24, 512, 3, 10),
+        "w1024": (2, 16, 1024, 1 << 15, 2, 19),
+        "odd_w5": (2, 21, 5, 256, 2, 7),
+    }.items():
+        layout = ref["VirtualKVLayout"](reqs, tokens, width, chunk_bytes=chunk)
+        n_elem = layout.capacity_bytes // layout.itemsize
+        raw_bits = torch.randint(0, 1 << 16, (n_elem,), generator=gen, dtype=torch.int32).to(torch.int16)
+        raw = raw_bits.view(torch.bfloat16)
+        request_ids = torch.randperm(reqs, generator=gen)[:batch].to(torch.int64)
+        lengths = torch.randint(1, tokens + 1, (batch,), generator=gen).to(torch.int64)
+        positions = torch.randint(-2, tokens + 2, (batch, selected), generator=gen).to(torch.int64)
+        count = reqs * tokens
+        table = torch.randperm(count, generator=gen).reshape(reqs, tokens).to(torch.int64) + 1
+        flat = torch.arange(count, dtype=torch.int64)
+        addresses = (layout.chunk_bytes // layout.itemsize
+                     + (flat // tokens) * (layout.request_bytes // layout.itemsize)
+                     + (flat % tokens) * width)
+        offsets = torch.zeros(count + 1, dtype=torch.int64)
+        offsets[table.flatten()] = addresses
+        record = dict(raw=raw_bits.numpy().view(np.uint16), positions=positions.numpy(),
+                      request_ids=request_ids.numpy(), lengths=lengths.numpy(),
+                      request_table=table.numpy(), slot_offsets=offsets.numpy(),
+                      layout=np.array([reqs, tokens, width, layout.itemsize, chunk], dtype=np.int64))
+        for indirect in (False, True):
+            out = torch.full((batch, selected, width), 7.0, dtype=torch.bfloat16)
+            ref["gather_rows"](raw, positions, request_ids, lengths, table, offsets, out, layout,
+                               indirect=indirect)
+            record["expected_indirect" if indirect else "expected_direct"] = (
+                out.view(torch.int16).numpy().view(np.uint16))
+        cases[name] = record
+    return cases
+
+
+def layout_cases(ref):
+    out = []
+    rng = random.Random(5)
+    for _ in range(12):
+        fields = dict(max_requests=rng.randint(1, 5), max_tokens=rng.randint(1, 40),
+                      row_elements=rng.randint(1, 9), itemsize=rng.choice([1, 2, 4]),
+                      chunk_bytes=rng.choice([8, 16, 64, 256]))
+        layout = ref["VirtualKVLayout"](**fields)
+        req = rng.randrange(fields["max_requests"])
+        length = rng.randint(0, fields["max_tokens"])
+        positions = [rng.randrange(fields["max_tokens"]) for _ in range(rng.randint(0, 5))]
+        out.append(dict(fields=fields, row_bytes=layout.row_bytes, request_bytes=layout.request_bytes,
+                        capacity_bytes=layout.capacity_bytes, req=req, length=length,
+                        request_offset=layout.request_offset(req),
+                        token_offsets=[layout.token_offset(req, p) for p in positions],
+                        positions=positions,
+                        prefix_chunks=sorted(layout.prefix_chunks(req, length)),
+                        selected_chunks=sorted(layout.selected_chunks(req, positions))))
+    return out
+
+
+class _FakeBacking:
+    def __init__(self):
+        self.mapped_chunks = set()
+        self.backed_bytes = 0
+
+    def ensure(self, indices):
+        self.mapped_chunks.update(indices)
+
+    def reclaim(self, indices, *, synchronize):
+        self.mapped_chunks.difference_update(indices)
+        return len(indices)
+
+
+def releasable_cases(ref):
+    sb = ref["scheduler_budget"]
+    rng = random.Random(137)
+    cases = []
+    for trial in range(40):
+        chunk_bytes = rng.choice([64, 256, 1024])
+        page_size = rng.choice([1, 2, 4])
+        row_choices = [8, 24, 40, 96, 128]
+        n_planes = rng.randint(1, 6)
+        page_count = rng.randint(4, 40)
+        planes = []
+        offset = 0
+        for _ in range(n_planes):
+            row = rng.choice(row_choices)
+            planes.append((offset // chunk_bytes, row))
+            length = (page_count + 1) * page_size * row
+            offset += -(-length // chunk_bytes) * chunk_bytes
+        n_chunks = offset // chunk_bytes
+        backing = _FakeBacking()
+        tracker = ref["PhysicalPages"](backing, page_size, page_count, planes, lambda: None,
+                                       chunk_bytes=chunk_bytes)
+        owned = rng.sample(range(1, page_count + 1), rng.randint(1, page_count))
+        tracker.acquire(owned)
+        if trial % 3 == 0:
+            # Some mapped chunks stop being mapped (partially reclaimed state).
+            drop = rng.sample(sorted(backing.mapped_chunks), len(backing.mapped_chunks) // 5)
+            backing.mapped_chunks.difference_update(drop)
+        candidates = [sorted(rng.sample(owned, rng.randint(1, len(owned)))) for _ in range(3)]
+        single = [sorted(sb._releasable(tracker, c)) for c in candidates]
+        counts = [sb._chunk_release_counts(tracker, set(c)) for c in candidates]
+        pair = sorted(sb._releasable_pair(tracker, set(candidates[0]), counts[0],
+                                          set(candidates[1]), counts[1]))
+        group = sorted(sb._releasable_group(tracker, [(set(c), k) for c, k in zip(candidates, counts)]))
+        cases.append(dict(chunk_bytes=chunk_bytes, page_size=page_size, page_count=page_count,
+                          planes=planes, n_chunks=n_chunks, owned=sorted(owned),
+                          refs={str(k): v for k, v in tracker.refs.items()},
+                          mapped=sorted(backing.mapped_chunks), candidates=candidates,
+                          page_chunks={str(p): sorted(tracker.chunks(p)) for p in [0, *owned]},
+                          releasable=single, pair=pair, group=group))
+    return cases
+
+
+def plans_fixture():
+    states = []
+    for rank in range(4):
+        path = REFERENCE / f"results/vmm-pair12k-shadow/adaptive_stats/plans-rank{rank:02d}.json"
+        states.append(json.loads(path.read_text())[0])
+    first = states[0]
+    identical = all(s == first for s in states[1:])
+    reduced = {key: first[key] for key in ("chunk_bytes", "page_size", "planes", "refs",
+                                           "mapped_chunks", "other_live_pages", "requests", "pairs")}
+    reduced["all_ranks_identical"] = identical
+    reduced["ranks"] = len(states)
+    return reduced
+
+
+def plan_demote_cases(ref):
+    migration = ref["migration"]
+    rng = random.Random(7)
+    cases = []
+    for trial in range(12):
+        chunk_bytes = rng.choice([64, 256])
+        page_size = rng.choice([1, 2])
+        planes = [(0, 40), (8, 24)] if trial % 2 else [(0, 96)]
+        backing = _FakeBacking()
+        tracker = ref["PhysicalPages"](backing, page_size, 60, planes, lambda: None, chunk_bytes=chunk_bytes)
+        pages = rng.sample(range(1, 61), rng.randint(2, 20))
+        others = [p for p in range(1, 61) if p not in pages]
+        tracker.acquire(pages + rng.sample(others, rng.randint(0, 10)))
+        keep = rng.randint(1, len(pages))
+        result = {}
+        for aware in ("0", "1"):
+            os.environ["EKV_CHUNK_AWARE_RETENTION"] = aware
+            retained, released = migration.plan_demote_pages(tracker, pages, keep)
+            result[aware] = [list(retained), list(released)]
+        os.environ.pop("EKV_CHUNK_AWARE_RETENTION", None)
+        cases.append(dict(chunk_bytes=chunk_bytes, page_size=page_size, planes=planes,
+                          owned=sorted(tracker.pages - {0}), pages=pages, keep=keep,
+                          plain=result["0"], aware=result["1"]))
+    return cases
+
+
+def main():
+    ref = _import_reference()
+    np.savez_compressed(HERE / "lookup_golden.npz",
+                        **{f"{case}__{key}": value for case, arrays in lookup_cases(ref).items()
+                           for key, value in arrays.items()})
+    np.savez_compressed(HERE / "gather_golden.npz",
+                        **{f"{case}__{key}": value for case, arrays in gather_cases(ref).items()
+                           for key, value in arrays.items()})
+    (HERE / "host_golden.json").write_text(json.dumps(
+        dict(layouts=layout_cases(ref), releasable=releasable_cases(ref),
+             plan_demote=plan_demote_cases(ref)), sort_keys=True))
+    (HERE / "plans_pair12k.json").write_text(json.dumps(plans_fixture(), sort_keys=True))
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+"""GPU parity of the Top-K row gather (R3) against the reference's golden vectors and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_npz_cases
+from oracle import gather as og
+
+pytestmark = pytest.mark.gpu
+
+
+def _layout_of(c):
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    reqs, tokens, width, itemsize, chunk = (int(v) for v in c["layout"])
+    return VirtualKVLayout(reqs, tokens, width, itemsize=itemsize, chunk_bytes=chunk)
+
+
+def _to(a, device, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(device)
+    return t if dtype is None else t.to(dtype)
+
+
+@pytest.mark.parametrize("case", sorted(load_npz_cases("gather_golden.npz")))
+@pytest.mark.parametrize("indirect", [False, True])
+def test_gather_rows_matches_reference(case, indirect, cuda_device):
+    from ekv_b200.sparse_read import gather_rows
+
+    c = load_npz_cases("gather_golden.npz")[case]
+    layout = _layout_of(c)
+    raw = _to(c["raw"].view(np.int16), cuda_device).view(torch.bfloat16)
+    positions = _to(c["positions"], cuda_device)
+    output = torch.full((*positions.shape, layout.row_elements), 7.0, dtype=torch.bfloat16,
+                        device=cuda_device)
+    gather_rows(raw, positions, _to(c["request_ids"], cuda_device), _to(c["lengths"], cuda_device),
+                _to(c["request_table"], cuda_device), _to(c["slot_offsets"], cuda_device), output,
+                layout, indirect=indirect)
+    torch.cuda.synchronize()
+    got = output.view(torch.int16).cpu().numpy().view(np.uint16)
+    np.testing.assert_array_equal(got, c["expected_indirect" if indirect else "expected_direct"])
+
+
+def test_gather_rows_contract(cuda_device):
+    from ekv_b200.sparse_read import gather_rows
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    layout = VirtualKVLayout(1, 4, 8)
+    dev = cuda_device
+    raw = torch.zeros(layout.capacity_bytes // 2, dtype=torch.bfloat16, device=dev)
+    idx = torch.zeros((1, 2), dtype=torch.int64, device=dev)
+    one = torch.ones(1, dtype=torch.int64, device=dev)
+    with pytest.raises(ValueError, match="output shape"):
+        gather_rows(raw, idx, one, one, idx, one, torch.empty((1, 2, 7), dtype=torch.bfloat16, device=dev),
+                    layout, indirect=False)
+    # Empty selection returns without touching the output.
+    empty = torch.zeros((1, 0), dtype=torch.int64, device=dev)
+    gather_rows(raw, empty, one, one, idx, one, torch.empty((1, 0, 8), dtype=torch.bfloat16, device=dev),
+                layout, indirect=False)
+    with pytest.raises(TypeError):
+        gather_rows(raw, idx, one, one, idx, one, torch.empty((1, 2, 8), dtype=torch.float32, device=dev),
+                    layout, indirect=False)
+
+
+@pytest.mark.parametrize("width,itemsize_dtype", [(1024, torch.bfloat16), (128, torch.bfloat16),
+                                                  (3, torch.bfloat16), (64, torch.float32),
+                                                  (17, torch.uint8)])
+def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, cuda_device):
+    from ekv_b200.sparse_read import gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    gen = torch.Generator().manual_seed(width)
+    slots, batch, selected, n_planes, tokens = 4096, 6, 300, 5, 512
+    esize = torch.empty((), dtype=itemsize_dtype).element_size()
+    layout = VirtualKVLayout(batch, tokens, width, itemsize=esize)
+    planes_cpu = [torch.randint(0, 256, (slots * width * esize,), generator=gen, dtype=torch.int32)
+                  .to(torch.uint8).view(itemsize_dtype) for _ in range(n_planes)]
+    table = torch.randint(0, slots, (batch, tokens), generator=gen)
+    slot_offsets = torch.arange(slots, dtype=torch.int64) * width
+    positions = torch.randint(-2, tokens + 2, (batch, selected), generator=gen)
+    lengths = torch.randint(tokens // 2, tokens + 1, (batch,), generator=gen)
+    request_ids = torch.randperm(batch, generator=gen)
+    planes = [p.to(cuda_device) for p in planes_cpu]
+    outputs = [torch.full((batch, selected, width), 3, dtype=itemsize_dtype, device=cuda_device)
+               for _ in range(n_planes)]
+    gather_rows_planes(planes, positions.to(cuda_device), request_ids.to(cuda_device),
+                       lengths.to(cuda_device), table.to(cuda_device), slot_offsets.to(cuda_device),
+                       outputs, layout, indirect=True)
+    torch.cuda.synchronize()
+    raw_views = [p.view(torch.uint8).numpy().view({1: np.uint8, 2: np.uint16, 4: np.uint32}[esize])
+                 for p in planes_cpu]
+    expected = og.gather_rows_planes(raw_views, positions.numpy(), request_ids.numpy(), lengths.numpy(),
+                                     table.numpy(), slot_offsets.numpy(), width=width,
+                                     table_width=tokens, request_stride=0, sink_elements=0,
+                                     indirect=True)
+    for out, exp in zip(outputs, expected):
+        np.testing.assert_array_equal(out.cpu().view(torch.uint8).numpy().view(exp.dtype), exp)
+
+
+def test_gather_rows_planes_more_planes_than_one_launch(cuda_device):
+    """300 planes: split into EKV_MAX_PLANES-sized launches."""
+    from ekv_b200.sparse_read import gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    n_planes, slots, width = 300, 64, 8
+    layout = VirtualKVLayout(1, slots, width)
+    planes = [torch.full((slots * width,), p, dtype=torch.int16, device=cuda_device).view(torch.bfloat16)
+              for p in range(n_planes)]
+    outputs = [torch.zeros((1, 4, width), dtype=torch.bfloat16, device=cuda_device) for _ in range(n_planes)]
+    positions = torch.tensor([[0, 5, 63, 64]], device=cuda_device)
+    one = torch.ones(1, dtype=torch.int64, device=cuda_device)
+    lengths = torch.full((1,), slots, dtype=torch.int64, device=cuda_device)
+    table = torch.arange(slots, device=cuda_device).view(1, slots)
+    offsets = torch.arange(slots, device=cuda_device) * width
+    gather_rows_planes(planes, positions, one * 0, lengths, table, offsets, outputs, layout, indirect=True)
+    torch.cuda.synchronize()
+    for p, out in enumerate(outputs):
+        vals = out.view(torch.int16)
+        assert (vals[0, :3] == p).all() and (vals[0, 3] == 0).all()
+
+
+def test_gather_full_config2_property(cuda_device):
+    """Config 2 at full size (36 layers x K,V pools [262144, 8, 128] bf16, 64 requests x
+    2048 Top-K slots): every gathered word identifies its plane, slot and column."""
+    from ekv_b200.sparse_read import gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    slots, width, layers, batch, topk = 262144, 1024, 36, 64, 2048
+    n_planes = 2 * layers
+    words = width // 2  # int32 words per row
+    layout = VirtualKVLayout(batch, topk, width)
+    base = torch.arange(slots * words, dtype=torch.int32, device=cuda_device).view(slots, words)
+    keys = [(p * 0x9E3779B1) & 0x7FFFFFFF for p in range(n_planes)]
+    planes = [torch.bitwise_xor(base, key) for key in keys]
+    del base
+    gen = torch.Generator(device=cuda_device).manual_seed(2)
+    table = torch.stack([torch.randperm(slots, generator=gen, device=cuda_device)[:topk]
+                         for _ in range(batch)])
+    positions = torch.stack([torch.randperm(topk, generator=gen, device=cuda_device)
+                             for _ in range(batch)])
+    request_ids = torch.arange(batch, device=cuda_device)
+    lengths = torch.full((batch,), topk, dtype=torch.int64, device=cuda_device)
+    positions[3, 7] = -1
+    positions[5, 9] = topk
+    offsets = torch.arange(slots, dtype=torch.int64, device=cuda_device) * width
+    outputs = [torch.empty((batch, topk, width), dtype=torch.bfloat16, device=cuda_device)
+               for _ in range(n_planes)]
+    gather_rows_planes([p.view(torch.bfloat16) for p in planes], positions, request_ids, lengths, table,
+                       offsets, outputs, layout, indirect=True)
+    torch.cuda.synchronize()
+    valid = (positions >= 0) & (positions < topk)
+    slot = torch.gather(table, 1, positions.clamp(0, topk - 1))
+    expect_words = slot[..., None].to(torch.int32) * words + torch.arange(words, device=cuda_device,
+                                                                           dtype=torch.int32)
+    for p, out in enumerate(outputs):
+        got = out.view(torch.int32)
+        ok = torch.where(valid[..., None], (got ^ keys[p]) == expect_words, got == 0)
+        assert bool(ok.all()), f"plane {p} mismatch"

@@ -1,0 +1,84 @@
+"""The chunked VMM backing on a real device: commit, zero fill, view, reclaim, recommit, ABI."""
+
+from __future__ import annotations
+
+import ctypes as ct
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+CHUNK = 2 << 20
+
+
+def test_backing_lifecycle(cuda_device):
+    from ekv_b200.backing import Backing
+
+    backing = Backing(10 * CHUNK + 123, CHUNK, device=cuda_device.index)
+    try:
+        assert backing.reserved_bytes == 11 * CHUNK and backing.granularity <= CHUNK
+        assert backing.base % CHUNK == 0 and backing.backed_bytes == 0
+        with pytest.raises(RuntimeError, match="sink"):
+            backing.raw
+        assert backing.ensure({0, 3, 4}) == 3
+        assert backing.backed_bytes == 3 * CHUNK
+        raw = backing.raw
+        assert raw.data_ptr() == backing.base and raw.numel() == backing.capacity_bytes
+        assert raw.device == cuda_device
+        assert not raw[3 * CHUNK:5 * CHUNK].any()  # zero-filled on commit
+        raw[3 * CHUNK:5 * CHUNK].fill_(0xAB)
+        torch.cuda.synchronize()
+        assert backing.reclaim({4}) == 1 and backing.backed_bytes == 2 * CHUNK
+        assert int(raw[3 * CHUNK]) == 0xAB
+        assert backing.ensure({4}) == 1
+        assert not raw[4 * CHUNK:5 * CHUNK].any()  # a recommitted chunk is fresh memory
+        assert backing.precommit({7, 8}) == 2
+        assert backing.mapped_chunks == {0, 3, 4}
+        assert backing.ensure({7}) == 0 and backing.mapped_chunks == {0, 3, 4, 7, 8}
+        assert not raw[7 * CHUNK:9 * CHUNK].any()
+        with pytest.raises(ValueError):
+            backing.ensure({11})
+        del raw
+    finally:
+        torch.cuda.synchronize()
+        backing.close()
+    with pytest.raises(RuntimeError):
+        backing.ensure({1})
+
+
+def test_backing_rejects_unaligned_chunk(cuda_device):
+    from ekv_b200.backing import Backing
+
+    with pytest.raises(RuntimeError, match="granularity"):
+        Backing(8 * CHUNK, CHUNK + 4096, device=cuda_device.index)
+
+
+def test_reference_ctypes_binding_loads_this_library(cuda_device, library_path):
+    """Bind the ev_* ABI with the argument types of elastic_kv/backing.py:19-52."""
+    lib = ct.CDLL(str(library_path))
+    lib.ev_create.argtypes = [ct.c_int, ct.c_uint64, ct.c_uint64]
+    lib.ev_create.restype = ct.c_void_p
+    for name in ("ev_ensure", "ev_precommit", "ev_drop"):
+        fn = getattr(lib, name)
+        fn.argtypes = [ct.c_void_p, ct.POINTER(ct.c_uint64), ct.c_size_t]
+        fn.restype = ct.c_int
+    for name in ("ev_base", "ev_backed", "ev_reserved", "ev_granularity"):
+        fn = getattr(lib, name)
+        fn.argtypes = [ct.c_void_p]
+        fn.restype = ct.c_uint64
+    lib.ev_poisoned.argtypes = [ct.c_void_p]
+    lib.ev_poisoned.restype = ct.c_int
+    lib.ev_close.argtypes = [ct.c_void_p]
+    lib.ev_close.restype = ct.c_int
+    lib.ev_error.restype = ct.c_char_p
+    handle = lib.ev_create(cuda_device.index, 4 * CHUNK, CHUNK)
+    assert handle, lib.ev_error()
+    ids = (ct.c_uint64 * 2)(2, 1)
+    assert lib.ev_ensure(handle, ids, 2) == 0
+    assert lib.ev_backed(handle) == 2 * CHUNK
+    bad = (ct.c_uint64 * 1)(9)
+    assert lib.ev_ensure(handle, bad, 1) == -1 and b"outside" in lib.ev_error()
+    assert lib.ev_poisoned(handle) == 0
+    assert lib.ev_drop(handle, ids, 2) == 0 and lib.ev_backed(handle) == 0
+    assert lib.ev_close(handle) == 0

@@ -1,0 +1,421 @@
+"""Host-side logic of the package, on CPU: layout, arena, page tracker, demotion
+planning, bitmap helpers, Backing error handling and the migration state machine."""
+
+from __future__ import annotations
+
+import ctypes as ct
+import os
+from types import SimpleNamespace
+from unittest.mock import Mock, call
+
+import pytest
+import torch
+
+from conftest import load_json
+from ekv_b200 import migration
+from ekv_b200.backing import Backing
+from ekv_b200.physical_pages import PhysicalPages
+from ekv_b200.releasable import bitmap_to_chunks, chunks_to_bitmap
+from ekv_b200.resident_arena import VmmResidentArena
+from ekv_b200.virtual_layout import VirtualKVLayout
+
+
+# ---------------------------------------------------------------- layout / arena
+
+@pytest.mark.parametrize("index", range(12))
+def test_layout_matches_reference(index):
+    case = load_json("host_golden.json")["layouts"][index]
+    layout = VirtualKVLayout(**case["fields"])
+    assert layout.row_bytes == case["row_bytes"]
+    assert layout.request_bytes == case["request_bytes"]
+    assert layout.capacity_bytes == case["capacity_bytes"]
+    assert layout.request_offset(case["req"]) == case["request_offset"]
+    assert [layout.token_offset(case["req"], p) for p in case["positions"]] == case["token_offsets"]
+    assert sorted(layout.prefix_chunks(case["req"], case["length"])) == case["prefix_chunks"]
+    assert sorted(layout.selected_chunks(case["req"], case["positions"])) == case["selected_chunks"]
+
+
+def test_layout_alignment_and_validation():
+    """Known answers of tests/test_virtual_layout.py:10-37."""
+    layout = VirtualKVLayout(2, 3, 3, chunk_bytes=8)
+    assert layout.capacity_bytes == 56 and layout.request_offset(1) == 32
+    assert layout.token_offset(0, 1) == 14
+    assert layout.prefix_chunks(0, 0) == set() and layout.selected_chunks(0, []) == set()
+    assert layout.selected_chunks(0, [1, 1]) == {1, 2}
+    assert layout.prefix_chunks(0, 3) == {1, 2, 3} and layout.prefix_chunks(1, 3) == {4, 5, 6}
+    fields = dict(max_requests=2, max_tokens=3, row_elements=3, itemsize=2, chunk_bytes=8)
+    for field in fields:
+        with pytest.raises(ValueError):
+            VirtualKVLayout(**(fields | {field: 0}))
+        with pytest.raises(TypeError):
+            VirtualKVLayout(**(fields | {field: True}))
+    layout = VirtualKVLayout(**fields)
+    for bad in (-1, 2):
+        with pytest.raises(ValueError):
+            layout.selected_chunks(bad, [])
+    for bad in (-1, 3):
+        with pytest.raises(ValueError):
+            layout.selected_chunks(0, [bad])
+    for bad in (-1, 4):
+        with pytest.raises(ValueError):
+            layout.prefix_chunks(0, bad)
+
+
+def test_arena_call_sequence():
+    """Same backing call sequence as tests/test_virtual_layout.py:49-65."""
+    calls = Mock()
+    layout = VirtualKVLayout(2, 5, 3, chunk_bytes=8)
+    arena = VmmResidentArena(layout, backing_factory=calls.factory, synchronize=calls.sync)
+    arena.reserve(0, 3)
+    arena.reserve(0, 1)
+    arena.reserve(1, 1)
+    arena.resize_quiescent(0, 2)
+    arena.close()
+    arena.close()
+    assert calls.mock_calls == [
+        call.factory(72, chunk_bytes=8, device=0), call.factory().ensure({0}),
+        call.factory().ensure({1, 2, 3}), call.factory().ensure({5}),
+        call.sync(), call.factory().reclaim({3}, synchronize=False),
+        call.sync(), call.factory().close(),
+    ]
+    with pytest.raises(RuntimeError):
+        arena.reserve(0, 1)
+
+
+def test_arena_failure_stops_use():
+    calls = Mock()
+    layout = VirtualKVLayout(2, 5, 3, chunk_bytes=8)
+    arena = VmmResidentArena(layout, backing_factory=calls.factory, synchronize=calls.sync)
+    calls.factory.return_value.ensure.side_effect = RuntimeError("allocation failed")
+    with pytest.raises(RuntimeError, match="allocation failed"):
+        arena.reserve(0, 2)
+    with pytest.raises(RuntimeError):
+        arena.row_view(0, 0, SimpleNamespace(itemsize=2))
+    arena.close()
+    calls.sync.assert_called_once()
+
+
+# ---------------------------------------------------------------- page tracker
+
+class FakeBacking:
+    def __init__(self):
+        self.mapped_chunks = set()
+        self.fail = False
+
+    @property
+    def backed_bytes(self):
+        return len(self.mapped_chunks) * 8
+
+    def ensure(self, indices):
+        if self.fail:
+            raise RuntimeError("map failed")
+        self.mapped_chunks.update(indices)
+
+    def reclaim(self, indices, *, synchronize):
+        assert not synchronize
+        self.mapped_chunks.difference_update(indices)
+        return len(indices)
+
+
+def test_physical_pages_known_answers():
+    """tests/test_minimax_vmm.py:27-51."""
+    backing = FakeBacking()
+    syncs = []
+    pages = PhysicalPages(backing, 2, 4, [(0, 3), (8, 2)], lambda: syncs.append(True), chunk_bytes=8)
+    assert pages.chunks(1) == {0, 1, 8}
+    pages.acquire([1, 2, 2])
+    pages.acquire([2])
+    pages.release({1})
+    assert pages.stats()["reclaimable_bytes"] == 0
+    pages.release({2})
+    assert pages.trim_quiescent() == 24
+    assert backing.mapped_chunks == {0, 8} and syncs == [True]
+    with pytest.raises(RuntimeError):
+        pages.release({0})
+    failing = FakeBacking()
+    tracker = PhysicalPages(failing, 1, 3, [(0, 8)], lambda: None, chunk_bytes=8)
+    failing.fail = True
+    with pytest.raises(RuntimeError, match="map failed"):
+        tracker.acquire([1])
+    assert tracker.pages == {0} and tracker.refs == {0: 1}
+
+
+@pytest.mark.parametrize("index", range(40))
+def test_physical_pages_projection_matches_reference(index):
+    case = load_json("host_golden.json")["releasable"][index]
+    tracker = PhysicalPages(FakeBacking(), case["page_size"], case["page_count"],
+                            [tuple(p) for p in case["planes"]], lambda: None,
+                            chunk_bytes=case["chunk_bytes"])
+    for page, chunks in case["page_chunks"].items():
+        assert sorted(tracker.chunks(int(page))) == chunks
+    tracker.acquire(case["owned"])
+    assert {str(k): v for k, v in tracker.refs.items()} == case["refs"]
+    assert tracker.n_chunks == case["n_chunks"]
+
+
+@pytest.mark.parametrize("index", range(12))
+def test_plan_demote_pages_matches_reference(index, monkeypatch):
+    case = load_json("host_golden.json")["plan_demote"][index]
+    tracker = PhysicalPages(FakeBacking(), case["page_size"], 60, [tuple(p) for p in case["planes"]],
+                            lambda: None, chunk_bytes=case["chunk_bytes"])
+    tracker.acquire(case["owned"])
+    monkeypatch.setenv("EKV_CHUNK_AWARE_RETENTION", "0")
+    kept, released = migration.plan_demote_pages(tracker, case["pages"], case["keep"])
+    assert [list(kept), list(released)] == case["plain"]
+    monkeypatch.setenv("EKV_CHUNK_AWARE_RETENTION", "1")
+    kept, released = migration.plan_demote_pages(tracker, case["pages"], case["keep"])
+    assert [list(kept), list(released)] == case["aware"]
+
+
+def test_plan_demote_pages_rejects_bad_input(monkeypatch):
+    monkeypatch.delenv("EKV_CHUNK_AWARE_RETENTION", raising=False)
+    for pages, keep in (([1, 2], 0), ([1, 2], 3), ([1, 1], 1)):
+        with pytest.raises(ValueError):
+            migration.plan_demote_pages(None, pages, keep)
+    monkeypatch.setenv("EKV_CHUNK_AWARE_RETENTION", "1")
+    with pytest.raises(RuntimeError):
+        migration.plan_demote_pages(None, [1, 2], 1)
+
+
+def test_bitmap_helpers_round_trip():
+    chunks = {0, 1, 63, 64, 127, 200, 4095}
+    bits = chunks_to_bitmap(chunks, 4096, "cpu")
+    assert bits.dtype == torch.int64 and bits.numel() == 64
+    assert bitmap_to_chunks(bits) == chunks
+    with pytest.raises(ValueError):
+        chunks_to_bitmap({4096}, 4096, "cpu")
+
+
+# ---------------------------------------------------------------- Backing with a fake ABI
+
+class FakeLibrary:
+    """Stands in for the ev_* ABI; can fail a call and report poisoning."""
+
+    def __init__(self):
+        self.calls = []
+        self.fail = None
+        self.poisoned = 0
+        self.error = b""
+        self.mapped = set()
+
+    def ev_create(self, device, capacity, chunk):
+        self.chunk = chunk
+        self.capacity = -(-capacity // chunk) * chunk
+        return 1234
+
+    def _ids(self, array, count):
+        return [array[i] for i in range(count)]
+
+    def _op(self, name, handle, array, count):
+        ids = self._ids(array, count)
+        self.calls.append((name, ids))
+        if self.fail == name:
+            self.error = f"{name} failed".encode()
+            return -1
+        if name == "ev_drop":
+            self.mapped.difference_update(ids)
+        else:
+            self.mapped.update(ids)
+        return 0
+
+    def ev_ensure(self, handle, array, count):
+        return self._op("ev_ensure", handle, array, count)
+
+    def ev_precommit(self, handle, array, count):
+        return self._op("ev_precommit", handle, array, count)
+
+    def ev_drop(self, handle, array, count):
+        return self._op("ev_drop", handle, array, count)
+
+    def ev_base(self, handle):
+        return 1 << 40
+
+    def ev_reserved(self, handle):
+        return self.capacity
+
+    def ev_granularity(self, handle):
+        return self.chunk
+
+    def ev_backed(self, handle):
+        return len(self.mapped) * self.chunk
+
+    def ev_poisoned(self, handle):
+        return self.poisoned
+
+    def ev_error(self):
+        return self.error
+
+    def ev_close(self, handle):
+        self.calls.append(("ev_close", []))
+        return 0
+
+
+def test_backing_batches_and_metrics():
+    lib = FakeLibrary()
+    backing = Backing(10 << 20, 2 << 20, device=0, library=lib)
+    assert backing.reserved_bytes == 10 << 20
+    assert backing.ensure({3, 1, 1}) == 2
+    assert backing.ensure({1}) == 0
+    assert backing.precommit({4}) == 1
+    assert backing.mapped_chunks == {1, 3}
+    assert backing.ensure({4}) == 0 and backing.mapped_chunks == {1, 3, 4}
+    assert backing.reclaim({3, 2}, synchronize=False) == 1
+    assert lib.calls == [("ev_ensure", [1, 3]), ("ev_precommit", [4]), ("ev_ensure", []),
+                         ("ev_drop", [3])]
+    assert backing.metrics["ensure_chunks"] == 2 and backing.metrics["reclaim_chunks"] == 1
+    with pytest.raises(ValueError):
+        backing.ensure({5})
+    backing.close()
+    assert lib.calls[-1] == ("ev_close", [])
+    with pytest.raises(RuntimeError):
+        backing.ensure({1})
+
+
+def test_backing_clean_failure_stays_usable_and_poison_stops_it():
+    lib = FakeLibrary()
+    backing = Backing(8 << 20, 2 << 20, device=0, library=lib)
+    lib.fail = "ev_ensure"
+    with pytest.raises(RuntimeError, match="ev_ensure failed"):
+        backing.ensure({1})
+    assert backing.mapped_chunks == set()
+    lib.fail = None
+    assert backing.ensure({1}) == 1
+    lib.fail, lib.poisoned = "ev_drop", 1
+    with pytest.raises(RuntimeError, match="ev_drop failed"):
+        backing.reclaim({1}, synchronize=False)
+    with pytest.raises(RuntimeError, match="closed or has encountered"):
+        backing.ensure({2})
+
+
+def test_backing_rejects_bad_arguments():
+    lib = FakeLibrary()
+    with pytest.raises(ValueError):
+        Backing(0, 2 << 20, library=lib)
+    with pytest.raises(ValueError):
+        Backing(1 << 20, 2 << 20, device="cpu", library=lib)
+
+
+# ---------------------------------------------------------------- migration state machine
+
+def _coordinator(length=8, capacity=4, page_size=2):
+    rows = 3
+    host_calls = []
+
+    class HostPool:
+        def alloc_paged_token_slots(self, table, allocated, row, start, end):
+            table[row, start:end] = torch.arange(start, end)
+            allocated[row] = end
+            return table[row, :end]
+
+        def backup_from_device_all_layer(self, pool, host, physical, io_backend):
+            host_calls.append(("backup", host.tolist(), physical.tolist(), io_backend))
+
+        def allocated_host_indices(self, table, row, n):
+            return table[row, :int(n)]
+
+        def free(self, indices):
+            host_calls.append(("free", indices.tolist()))
+
+    physical = torch.arange(2, 2 + length, dtype=torch.int64)  # page-aligned, pages 1..4
+    device_pool = SimpleNamespace(
+        page_size=page_size,
+        translate_loc_from_full_to_hisparse_device=lambda logical: physical.clone(),
+        full_to_hisparse_device_index_mapping=torch.arange(64, dtype=torch.int64),
+        start_layer=0, end_layer=1)
+    coordinator = SimpleNamespace(
+        is_m3_hisparse=True, spec_swap=SimpleNamespace(enabled=False, reset=lambda row: None),
+        padded_buffer_size=capacity, device_buffer_size=capacity,
+        req_device_buffer_size=torch.zeros(rows, dtype=torch.int64),
+        req_to_host_pool=torch.full((rows, 16), -1, dtype=torch.int64),
+        req_to_host_pool_allocated_len=torch.zeros(rows, dtype=torch.int64),
+        req_to_token_pool=SimpleNamespace(req_to_token=torch.arange(rows * 16).reshape(rows, 16)),
+        mem_pool_device=device_pool, mem_pool_host=HostPool(),
+        wait_for_pending_backup=lambda: None,
+        token_to_kv_pool_allocator=SimpleNamespace(_kvcache=SimpleNamespace(),
+                                                   free_hisparse_indices=Mock()),
+        req_to_device_buffer=torch.zeros((rows, 16), dtype=torch.int64),
+        req_device_buffer_tokens=torch.zeros((1, rows, 16), dtype=torch.int64),
+        req_device_buffer_token_locs=torch.zeros((1, rows, 16), dtype=torch.int64),
+        lru_slots=torch.zeros((1, rows, 4), dtype=torch.int64), _lru_init=torch.arange(4),
+        _skip_first_backup=[False] * rows)
+    request = SimpleNamespace(kv=SimpleNamespace(req_pool_idx=1, kv_committed_len=length,
+                                                 kv_allocated_len=length),
+                              hisparse_staging=False)
+    return coordinator, request, host_calls
+
+
+def test_demotion_transaction_state_machine(monkeypatch):
+    monkeypatch.delenv("EKV_CHUNK_AWARE_RETENTION", raising=False)
+    coordinator, request, host_calls = _coordinator()
+    syncs = []
+    prepared = migration.prepare_demote(coordinator, request, lambda: syncs.append(1))
+    assert prepared.status == "prepared"
+    assert prepared.retained_rows == (0, 1) and prepared.released_rows == (2, 3)
+    assert host_calls[0][0] == "backup" and host_calls[0][2] == list(range(2, 10))
+    published = []
+    released = migration.commit_demote(prepared, published.append, lambda: None)
+    assert released == 0 and published == [1] and prepared.status == "committed"
+    assert coordinator.req_to_device_buffer[1, :4].tolist() == [2, 3, 4, 5]
+    assert coordinator._skip_first_backup[1] is True
+    freed = coordinator.token_to_kv_pool_allocator.free_hisparse_indices.call_args[0][0]
+    assert freed.tolist() == [6, 8]
+    with pytest.raises(RuntimeError):
+        migration.commit_demote(prepared, published.append, lambda: None)
+    with pytest.raises(RuntimeError):
+        migration.abort_demote(prepared)
+
+
+def test_demotion_abort_and_rejections(monkeypatch):
+    monkeypatch.delenv("EKV_CHUNK_AWARE_RETENTION", raising=False)
+    coordinator, request, host_calls = _coordinator()
+    prepared = migration.prepare_demote(coordinator, request, lambda: None)
+    migration.abort_demote(prepared)
+    assert prepared.status == "aborted" and host_calls[-1][0] == "free"
+    assert int(coordinator.req_to_host_pool_allocated_len[1]) == 0
+    short, short_request, _ = _coordinator(length=2, capacity=4)
+    with pytest.raises(ValueError):
+        migration.prepare_demote(short, short_request, lambda: None)
+    coordinator, request, _ = _coordinator()
+    coordinator.spec_swap.enabled = True
+    with pytest.raises(RuntimeError):
+        migration.prepare_demote(coordinator, request, lambda: None)
+
+
+def test_profile_ranges_env_is_read_at_decoration(monkeypatch):
+    from ekv_b200.profile_ranges import profile_range
+
+    def fn():
+        return 3
+
+    monkeypatch.delenv("EKV_PROFILE_RANGES", raising=False)
+    assert profile_range("x")(fn) is fn
+    monkeypatch.setenv("EKV_PROFILE_RANGES", "1")
+    wrapped = profile_range("x")(fn)
+    assert wrapped is not fn and wrapped() == 3
+
+
+def test_no_cpu_fallback_without_cuda_tensors():
+    from ekv_b200.resident_lookup import lookup_slots, resolve_resident
+
+    x = torch.zeros((1, 2, 3), dtype=torch.int32)
+    with pytest.raises(ValueError, match="CUDA"):
+        resolve_resident(x, torch.zeros((2, 3), dtype=torch.int32), torch.zeros(3, dtype=torch.int64),
+                         torch.zeros(2, dtype=torch.int64), torch.zeros(2, dtype=torch.int32),
+                         torch.zeros(1, dtype=torch.int64), torch.zeros((1, 2, 3), dtype=torch.int32), 1)
+    with pytest.raises(ValueError, match="CUDA"):
+        lookup_slots(torch.zeros((2, 4), dtype=torch.int32), torch.zeros((2, 3), dtype=torch.int32))
+
+
+def test_library_missing_fails_loudly(tmp_path):
+    from ekv_b200 import _lib
+
+    with pytest.raises(RuntimeError, match="no fallback"):
+        _lib.library(str(tmp_path / "missing.so"))
+
+
+def test_ctypes_arrays():
+    from ekv_b200._lib import i64_array, u64_array
+
+    assert list(u64_array([1, 2])) == [1, 2]
+    assert isinstance(i64_array([]), ct.Array)
+    assert os.path.basename(str(__file__)).startswith("test_")

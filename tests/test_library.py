@@ -1,0 +1,63 @@
+"""The C-ABI library loads without a GPU and exports every symbol include/*.h declares."""
+
+from __future__ import annotations
+
+import ctypes as ct
+import re
+from conftest import ROOT
+
+_DECL = re.compile(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*\b((?:ekv|ev)_[a-z0-9_]+)\s*\(",
+                   re.MULTILINE)
+
+
+def declared_symbols():
+    names = set()
+    for header in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.DOTALL)
+        names.update(_DECL.findall(text))
+    return names
+
+
+def test_headers_declare_the_full_abi():
+    names = declared_symbols()
+    assert {"ekv_error", "ekv_resolve_resident", "ekv_lookup_slots", "ekv_gather_rows",
+            "ekv_gather_rows_planes", "ekv_pack_rows", "ekv_unpack_rows", "ekv_chunk_counts",
+            "ekv_freeable_bitmap", "ekv_bitmap_and", "ev_create", "ev_ensure", "ev_precommit",
+            "ev_drop", "ev_base", "ev_backed", "ev_reserved", "ev_granularity", "ev_poisoned",
+            "ev_error", "ev_close"} <= names
+
+
+def test_library_exports_every_declared_symbol(library_path):
+    lib = ct.CDLL(str(library_path))
+    missing = [name for name in sorted(declared_symbols()) if not hasattr(lib, name)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_the_headers(library_path):
+    from ekv_b200 import _lib
+
+    assert set(_lib.EXPORTS) == declared_symbols()
+    lib = _lib.library(str(library_path))
+    assert lib.ekv_abi_version() == 1
+    assert lib.ekv_error() == b""
+
+
+def test_entry_points_validate_before_touching_a_device(library_path):
+    """Argument errors come back as -1 plus a message, with no GPU present."""
+    from ekv_b200 import _lib
+
+    lib = _lib.library(str(library_path))
+    rc = lib.ekv_bitmap_and(None, 0, 4, None, 0, None)
+    assert rc == -1 and b"rank" in lib.ekv_error()
+    rc = lib.ekv_gather_rows_planes(None, None, 0, 2, None, 4, None, 4, None, 4, None, 8, None, 8,
+                                    1, 1, 1, 1, 1, 0, 1, 0, None)
+    assert rc == -1 and b"plane count" in lib.ekv_error()
+    rc = lib.ekv_resolve_resident(None, 4, 0, 0, 1, None, 4, 0, 0, None, 8, 0, None, 8, 0, None, 4, 0,
+                                  None, 8, 0, 1, None, 0, 0, 0, 0, None)
+    assert rc == -1 and b"block_size" in lib.ekv_error()
+    # Empty work is a successful no-op.
+    assert lib.ekv_bitmap_and(None, 1, 0, None, 0, None) == 0
+    import torch
+
+    if not torch.cuda.is_available():
+        assert not lib.ev_create(0, 1 << 21, 1 << 21) and lib.ev_error()
