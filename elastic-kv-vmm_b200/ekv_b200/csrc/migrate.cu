@@ -116,11 +116,25 @@ int row_copy_impl(const uint64_t* planes, int n_planes, int64_t row_bytes, const
             require(n_tasks == static_cast<int64_t>(n_planes) * n_slots,
                     "cross form needs n_tasks == n_planes * n_slots");
         }
+        bind_device(device);
+        // Staging must be device memory or pinned host memory mapped into the
+        // device address space; anything else is refused here rather than
+        // faulting in the kernel.
+        cudaPointerAttributes attr{};
+        cuda_check(cudaPointerGetAttributes(&attr, staging), "query staging pointer");
+        void* staging_device = const_cast<void*>(staging);
+        if (attr.type == cudaMemoryTypeHost) {
+            require(attr.devicePointer != nullptr, "pinned staging is not mapped for device access");
+            staging_device = attr.devicePointer;
+        } else {
+            require(attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged,
+                    "staging must be device memory or pinned host memory");
+        }
         RowCopyParams p{};
         p.plane_index = plane_index;
         p.slots = slots;
         p.stage_rows = stage_rows;
-        p.staging = const_cast<char*>(static_cast<const char*>(staging));
+        p.staging = static_cast<char*>(staging_device);
         p.stage_plane_stride = stage_plane_stride_bytes;
         p.row_bytes = row_bytes;
         p.n_slots = n_slots;
@@ -129,7 +143,7 @@ int row_copy_impl(const uint64_t* planes, int n_planes, int64_t row_bytes, const
         p.stage_es = stage_rows ? stage_rows_esize : 8;
         p.n_planes = n_planes;
         p.to_staging = to_staging;
-        uint64_t addr_or = reinterpret_cast<uint64_t>(staging) |
+        uint64_t addr_or = reinterpret_cast<uint64_t>(staging_device) |
                            static_cast<uint64_t>(stage_plane_stride_bytes);
         for (int i = 0; i < n_planes; ++i) {
             require(planes[i], "null plane address");
