@@ -60,6 +60,9 @@ def parse_args(argv=None):
     p.add_argument("--skip-migration", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
+    p.add_argument("--tp-shard", type=int, default=0,
+                   help="measurement aid: gather one rank's head shard of TP=N on this GPU "
+                        "(default: the launch's world size)")
     return p.parse_args(argv)
 
 
@@ -197,16 +200,17 @@ def timed(fn, steps, warmup, dist: Dist):
 class Workload:
     """Config-2 pool (VMM-backed) and Top-K indices for this rank's head shard."""
 
-    def __init__(self, dist: Dist, layers: int):
+    def __init__(self, dist: Dist, layers: int, shard: int = 0):
         from ekv_b200.backing import Backing
         from ekv_b200.virtual_layout import VirtualKVLayout
 
-        if CFG2["kv_heads"] % dist.world:
-            raise SystemExit("--gpus must divide the 8 KV heads")
+        shard = shard or dist.world
+        if CFG2["kv_heads"] % shard:
+            raise SystemExit("--gpus / --tp-shard must divide the 8 KV heads")
         self.dist = dist
         dev = dist.device
         self.layers = layers
-        self.heads = CFG2["kv_heads"] // dist.world
+        self.heads = CFG2["kv_heads"] // shard
         self.width = self.heads * CFG2["head_dim"]             # elements per row (this rank)
         self.row_bytes = self.width * 2
         self.slots = CFG2["slots"]
@@ -451,7 +455,7 @@ def bitmap_bench(dist: Dist, reps: int = 50):
 def run_ours(args, dist: Dist):
     from ekv_b200.sparse_read import gather_rows_planes
 
-    work = Workload(dist, args.layers)
+    work = Workload(dist, args.layers, args.tp_shard)
     gather = work.plane_gather()
     with ClockSampler(dist.local_rank) as clocks:
         ms = timed(gather, args.steps, args.warmup, dist)

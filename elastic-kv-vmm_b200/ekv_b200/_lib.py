@@ -80,6 +80,7 @@ _KERNELS = {
     ],
     "ekv_freeable_bitmap": [_p, _p, _p, _i64, _p, _i32, _p],
     "ekv_bitmap_and": [_p, _i32, _i64, _p, _i32, _p],
+    "ekv_device_status": [_i32, ct.POINTER(ct.c_uint), _i32],
 }
 
 _VMM = {
@@ -134,6 +135,14 @@ def call(name: str, *args) -> None:
     lib = library()
     if getattr(lib, name)(*args) != 0:
         raise KernelError(f"{name}: {lib.ekv_error().decode('utf-8', 'replace')}")
+
+
+def device_status(device, clear: bool = True) -> int:
+    """Sticky status word of ``device`` (0 = every bounded wait completed); synchronous."""
+    index = torch.device(device).index if not isinstance(device, int) else device
+    status = ct.c_uint(0)
+    call("ekv_device_status", 0 if index is None else index, ct.byref(status), int(clear))
+    return status.value
 
 
 def u64_array(values) -> ct.Array:

@@ -38,6 +38,13 @@ const char* ekv_error(void);
 int ekv_abi_version(void);
 
 /*
+ * Sticky device-side status of `device`: non-zero when a kernel abandoned a
+ * bounded wait (its output is then incomplete).  Synchronous; `clear` resets
+ * it.  No reference counterpart (the reference's Triton kernels never wait).
+ */
+int ekv_device_status(int device, unsigned int* status, int clear);
+
+/*
  * R1 — resident lookup.  Replaces the Triton `_resolve` launch of
  * resolve_resident (adaptive_sparse/resident_lookup.py:6-40).
  * For every s < n_selected, row = selected[s], and every column j < width

@@ -12,6 +12,18 @@ from oracle import gather as og
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["bulk", "vector"])
+def gather_kernel(request, monkeypatch, cuda_device):
+    """Run a test with the bulk (TMA-engine) kernel, then with the register-staged one."""
+    from ekv_b200._lib import device_status
+
+    monkeypatch.setenv("EKV_GATHER_KERNEL", request.param)
+    device_status(cuda_device, clear=True)
+    yield request.param
+    torch.cuda.synchronize()
+    assert device_status(cuda_device, clear=True) == 0, "a bounded wait was abandoned"
+
+
 def _layout_of(c):
     from ekv_b200.virtual_layout import VirtualKVLayout
 
@@ -26,7 +38,7 @@ def _to(a, device, dtype=None):
 
 @pytest.mark.parametrize("case", sorted(load_npz_cases("gather_golden.npz")))
 @pytest.mark.parametrize("indirect", [False, True])
-def test_gather_rows_matches_reference(case, indirect, cuda_device):
+def test_gather_rows_matches_reference(case, indirect, gather_kernel, cuda_device):
     from ekv_b200.sparse_read import gather_rows
 
     c = load_npz_cases("gather_golden.npz")[case]
@@ -67,7 +79,7 @@ def test_gather_rows_contract(cuda_device):
 @pytest.mark.parametrize("width,itemsize_dtype", [(1024, torch.bfloat16), (128, torch.bfloat16),
                                                   (3, torch.bfloat16), (64, torch.float32),
                                                   (17, torch.uint8)])
-def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, cuda_device):
+def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, gather_kernel, cuda_device):
     from ekv_b200.sparse_read import gather_rows_planes
     from ekv_b200.virtual_layout import VirtualKVLayout
 
@@ -99,7 +111,7 @@ def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, cuda_device):
         np.testing.assert_array_equal(out.cpu().view(torch.uint8).numpy().view(exp.dtype), exp)
 
 
-def test_gather_rows_planes_more_planes_than_one_launch(cuda_device):
+def test_gather_rows_planes_more_planes_than_one_launch(gather_kernel, cuda_device):
     """300 planes: split into EKV_MAX_PLANES-sized launches."""
     from ekv_b200.sparse_read import gather_rows_planes
     from ekv_b200.virtual_layout import VirtualKVLayout
@@ -121,7 +133,7 @@ def test_gather_rows_planes_more_planes_than_one_launch(cuda_device):
         assert (vals[0, :3] == p).all() and (vals[0, 3] == 0).all()
 
 
-def test_gather_full_config2_property(cuda_device):
+def test_gather_full_config2_property(gather_kernel, cuda_device):
     """Config 2 at full size (36 layers x K,V pools [262144, 8, 128] bf16, 64 requests x
     2048 Top-K slots): every gathered word identifies its plane, slot and column."""
     from ekv_b200.sparse_read import gather_rows_planes
@@ -158,3 +170,32 @@ def test_gather_full_config2_property(cuda_device):
         got = out.view(torch.int32)
         ok = torch.where(valid[..., None], (got ^ keys[p]) == expect_words, got == 0)
         assert bool(ok.all()), f"plane {p} mismatch"
+
+
+def test_bulk_gather_falls_back_for_misaligned_rows(gather_kernel, cuda_device):
+    """16-byte aligned planes and row size, but some slot offsets land on odd elements:
+    those 32-row batches are copied with element loads, the rest with bulk copies."""
+    from ekv_b200.sparse_read import gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    gen = torch.Generator().manual_seed(77)
+    slots, width, batch, selected, tokens = 2048, 64, 4, 700, 1024
+    layout = VirtualKVLayout(batch, tokens, width)
+    planes_cpu = [torch.randint(-32768, 32767, (slots * width + 8,), generator=gen, dtype=torch.int16)
+                  for _ in range(3)]
+    offsets = torch.arange(slots, dtype=torch.int64) * width
+    offsets[torch.randperm(slots, generator=gen)[:20]] += 3  # a few rows start mid-vector
+    table = torch.randint(0, slots, (batch, tokens), generator=gen)
+    positions = torch.randint(-1, tokens, (batch, selected), generator=gen)
+    lengths = torch.full((batch,), tokens, dtype=torch.int64)
+    request_ids = torch.arange(batch)
+    outputs = [torch.empty((batch, selected, width), dtype=torch.bfloat16, device=cuda_device) for _ in planes_cpu]
+    gather_rows_planes([p.to(cuda_device).view(torch.bfloat16) for p in planes_cpu], positions.to(cuda_device),
+                       request_ids.to(cuda_device), lengths.to(cuda_device), table.to(cuda_device),
+                       offsets.to(cuda_device), outputs, layout, indirect=True)
+    torch.cuda.synchronize()
+    expected = og.gather_rows_planes([p.numpy() for p in planes_cpu], positions.numpy(), request_ids.numpy(),
+                                     lengths.numpy(), table.numpy(), offsets.numpy(), width=width,
+                                     table_width=tokens, request_stride=0, sink_elements=0, indirect=True)
+    for out, exp in zip(outputs, expected):
+        np.testing.assert_array_equal(out.view(torch.int16).cpu().numpy(), exp)
