@@ -162,6 +162,37 @@ int ekv_unpack_rows(
     int device, void* stream);
 
 /*
+ * R5, staged through the copy engines — the same task list (plane_index /
+ * slots / n_slots / n_tasks as above; no stage_rows) moved between the planes
+ * and PINNED host memory `host_staging` through a ring of four device slots cut
+ * from the caller's `scratch` device buffer (scratch_bytes >= 4 * 256-aligned
+ * slots of at least one row): the row-copy kernel packs / unpacks one slot on
+ * `stream` while `copy_stream` (NULL = an internal per-device stream) moves
+ * another across the host link with cudaMemcpyAsync.
+ * `segments` is a HOST array of n_segments triples (first_task, count,
+ * host_byte_offset): tasks [first_task, first_task + count) occupy consecutive
+ * rows of host_staging starting at host_byte_offset; segments are in task order
+ * and cover [0, n_tasks).  When `stream` completes, the transfer is complete.
+ * Calls on one device must not overlap.  Replaces the same reference call sites
+ * as ekv_pack_rows / ekv_unpack_rows.
+ */
+int ekv_pack_rows_staged(
+    const uint64_t* planes, int n_planes, int64_t row_bytes,
+    const int32_t* plane_index, const void* slots, int slots_esize, int64_t n_slots,
+    const int64_t* segments, int64_t n_segments,
+    void* host_staging, int64_t n_tasks,
+    void* scratch, int64_t scratch_bytes,
+    int device, void* stream, void* copy_stream);
+
+int ekv_unpack_rows_staged(
+    const uint64_t* planes, int n_planes, int64_t row_bytes,
+    const int32_t* plane_index, const void* slots, int slots_esize, int64_t n_slots,
+    const int64_t* segments, int64_t n_segments,
+    const void* host_staging, int64_t n_tasks,
+    void* scratch, int64_t scratch_bytes,
+    int device, void* stream, void* copy_stream);
+
+/*
  * R4/R6 — page -> chunk projection counts.  Restates PhysicalPages.chunks
  * (adaptive_sparse/minimax_vmm.py:40-52) and _chunk_release_counts
  * (adaptive_sparse/scheduler_budget.py:155-156): for each page and plane p,

@@ -171,3 +171,108 @@ def test_pinned_host_pool_backup_and_load(cuda_device):
             assert torch.equal(device_plane[dest], host_rows.to(cuda_device))
     assert pool.available_size() == 700
     assert pool.free(host) == 300 and pool.available_size() == 1000
+
+
+@pytest.mark.parametrize("row_bytes,scratch_bytes", [(2048, 64 << 20), (2048, 40 << 10), (48, 8 << 10),
+                                                     (256, 1 << 20)])
+def test_staged_cross_form_round_trip(row_bytes, scratch_bytes, cuda_device):
+    """Copy-engine transfers through a scratch ring (small rings force many wraps)."""
+    from ekv_b200.host_pool import pack_rows_staged, pinned_buffer, unpack_rows_staged
+
+    gen = torch.Generator().manual_seed(row_bytes + scratch_bytes)
+    n, rows, count = 3, 4000, 2500
+    planes = _planes(gen, n, rows, row_bytes, cuda_device)
+    slots = torch.randperm(rows, generator=gen)[:count].to(cuda_device)
+    plane_stride = 3000 * row_bytes
+    host = pinned_buffer(n * plane_stride)
+    host.fill_(0)
+    # Host rows of each plane: two runs (rows 10.. and 1500..), like a fragmented host pool.
+    segments = []
+    for p in range(n):
+        segments.append((p * count, 1200, p * plane_stride + 10 * row_bytes))
+        segments.append((p * count + 1200, count - 1200, p * plane_stride + 1500 * row_bytes))
+    scratch = torch.empty(scratch_bytes, dtype=torch.uint8, device=cuda_device)
+    pack_rows_staged(planes, slots, host, segments, scratch=scratch)
+    torch.cuda.synchronize()
+    host_rows = torch.cat([torch.arange(10, 1210), torch.arange(1500, 1500 + count - 1200)])
+    for p in range(n):
+        view = host[p * plane_stride:(p + 1) * plane_stride].view(3000, row_bytes)
+        assert torch.equal(view[host_rows], planes[p][slots].cpu())
+    fresh = [torch.zeros_like(pl) for pl in planes]
+    dest = torch.randperm(rows, generator=gen)[:count].to(cuda_device)
+    unpack_rows_staged(fresh, dest, host, segments, scratch=scratch)
+    torch.cuda.synchronize()
+    for p in range(n):
+        assert torch.equal(fresh[p][dest], planes[p][slots])
+        untouched = torch.ones(rows, dtype=torch.bool, device=cuda_device)
+        untouched[dest] = False
+        assert not fresh[p][untouched].any()
+
+
+def test_staged_list_form_chunk_aligned(cuda_device):
+    """Victim-chunk staging: each chunk's rows start on a 2 MiB boundary of pinned memory."""
+    from ekv_b200.host_pool import CHUNK_BYTES, pack_rows_staged, pinned_buffer, unpack_rows_staged
+
+    gen = torch.Generator().manual_seed(8)
+    n, rows, row_bytes = 4, 4096, 2048
+    per_chunk = CHUNK_BYTES // row_bytes
+    planes = _planes(gen, n, rows, row_bytes, cuda_device)
+    victims = [(0, 1), (2, 3), (3, 0), (1, 2)]  # (plane, chunk)
+    plane_index, src, segments, t = [], [], [], 0
+    for v, (plane, chunk) in enumerate(victims):
+        occupied = torch.nonzero(torch.rand(per_chunk, generator=gen) < 0.7).flatten()
+        plane_index.append(torch.full((occupied.numel(),), plane, dtype=torch.int32))
+        src.append(chunk * per_chunk + occupied)
+        segments.append((t, occupied.numel(), v * CHUNK_BYTES))
+        t += occupied.numel()
+    plane_index = torch.cat(plane_index).to(cuda_device)
+    src = torch.cat(src).to(cuda_device)
+    host = pinned_buffer(len(victims) * CHUNK_BYTES)
+    pack_rows_staged(planes, src, host, segments, plane_index=plane_index,
+                     scratch=torch.empty(1 << 20, dtype=torch.uint8, device=cuda_device))
+    torch.cuda.synchronize()
+    for (first, count, offset) in segments:
+        got = host[offset:offset + count * row_bytes].view(count, row_bytes)
+        idx = slice(first, first + count)
+        want = torch.stack([planes[int(p)][int(s)] for p, s in zip(plane_index[idx].tolist(), src[idx].tolist())])
+        assert torch.equal(got.to(cuda_device), want)
+    fresh = [torch.zeros_like(pl) for pl in planes]
+    unpack_rows_staged(fresh, src, host, segments, plane_index=plane_index)
+    torch.cuda.synchronize()
+    for p in range(n):
+        pick = plane_index == p
+        assert torch.equal(fresh[p][src[pick]], planes[p][src[pick]])
+
+
+def test_staged_rejects_bad_segments(cuda_device):
+    from ekv_b200._lib import KernelError
+    from ekv_b200.host_pool import pack_rows_staged, pinned_buffer
+
+    planes = [torch.zeros((64, 32), dtype=torch.uint8, device=cuda_device)]
+    slots = torch.arange(10, device=cuda_device)
+    host = pinned_buffer(1 << 20)
+    with pytest.raises(KernelError, match="cover"):
+        pack_rows_staged(planes, slots, host, [(0, 5, 0)])
+    with pytest.raises(KernelError, match="task order"):
+        pack_rows_staged(planes, slots, host, [(0, 5, 0), (6, 4, 4096)])
+    with pytest.raises(ValueError, match="pinned"):
+        pack_rows_staged(planes, slots, torch.zeros(1 << 20, dtype=torch.uint8), [(0, 10, 0)])
+
+
+def test_pinned_host_pool_fragmented_rows_use_zero_copy(cuda_device):
+    from ekv_b200.host_pool import PinnedHostKVPool
+
+    gen = torch.Generator().manual_seed(9)
+    slots, layers = 1024, 2
+    keys = [torch.randn((slots, 256), generator=gen).to(torch.bfloat16).to(cuda_device) for _ in range(layers)]
+    vals = [torch.randn((slots, 256), generator=gen).to(torch.bfloat16).to(cuda_device) for _ in range(layers)]
+    device_pool = SimpleNamespace(get_key_buffer=lambda l: keys[l], get_value_buffer=lambda l: vals[l],
+                                  start_layer=0, end_layer=layers)
+    pool = PinnedHostKVPool(2000, layers, 512, cuda_device)
+    host = torch.arange(0, 1200, 2)  # 600 runs of one row: more than MAX_STAGED_RUNS
+    physical = torch.randperm(slots, generator=gen)[:600].to(cuda_device)
+    pool.backup_from_device_all_layer(device_pool, host, physical)
+    torch.cuda.synchronize()
+    for layer in range(layers):
+        got = pool.plane_view(2 * layer + 1)[host].view(torch.bfloat16).view(600, 256)
+        assert torch.equal(got.to(cuda_device), vals[layer][physical])
