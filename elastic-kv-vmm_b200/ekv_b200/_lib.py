@@ -87,6 +87,13 @@ _KERNELS = {
         _p, _i64,
         _i32, _p, _p,
     ],
+    "ekv_pack_rows_staged_noalloc": [
+        _u64p, _i32, _i64,
+        _p, _p, _i32, _i64,
+        _i64p, _i64,
+        _p, _i64,
+        _i32, _p, _p,
+    ],
     "ekv_chunk_counts": [
         _p, _i32, _i64,
         _i64p, _i64p, _i32,

@@ -378,3 +378,56 @@ extern "C" int ekv_unpack_rows_staged(
                             n_segments, host_staging, n_tasks, scratch, scratch_bytes, 0, device, stream,
                             copy_stream);
 }
+
+// ---------------------------------------------------------------- staged demotion without allocation
+//
+// Some callers cannot allocate device memory at the moment they demote: a
+// serving engine that reserved all of HBM for its KV pool at start-up (the very
+// pressure that triggers a demotion leaves nothing to allocate from), a C / Go
+// / Java host that has no device allocator of its own, or code that must not
+// touch the allocator in the middle of a step.  ekv_pack_rows_staged_noalloc
+// stages through a ring that belongs to the library: a file-scope device array
+// of kStaticRingBytes (4 slots of 2 MiB) that every GPU loading the library
+// holds until the process exits.  Host code only handles its address, which is
+// looked up once per device with that device current (the first call on a
+// device does this, so make that first call before any stream capture).  All
+// calls share the ring: calls that overlap on the GPU race, and the ring keeps
+// the previous call's bytes (nothing in it needs to start at zero, since every
+// slot row is written before it is copied out).
+
+namespace {
+constexpr int64_t kStaticRingBytes = int64_t{8} << 20;
+std::mutex g_static_ring_mutex;
+void* g_static_ring_address[64] = {};
+}  // namespace
+
+static __device__ __align__(256) unsigned char ekv_static_staging_ring[kStaticRingBytes];
+
+extern "C" int ekv_pack_rows_staged_noalloc(
+    const uint64_t* planes, int n_planes, int64_t row_bytes,
+    const int32_t* plane_index, const void* slots, int slots_esize, int64_t n_slots,
+    const int64_t* segments, int64_t n_segments,
+    void* host_staging, int64_t n_tasks,
+    int device, void* stream, void* copy_stream) {
+    void* ring = nullptr;
+    const int status = ekv::guarded([&] {
+        ekv::require(row_bytes > 0 && row_bytes <= kStaticRingBytes / 4,
+                     "row_bytes is larger than a slot of the built-in staging ring (2 MiB); "
+                     "use ekv_pack_rows_staged with a caller-provided scratch buffer");
+        ekv::require(device >= 0 && device < 64, "device ordinal outside [0, 64)");
+        std::lock_guard<std::mutex> lock(g_static_ring_mutex);
+        if (!g_static_ring_address[device]) {
+            ekv::bind_device(device);
+            void* address = nullptr;
+            ekv::cuda_check(cudaGetSymbolAddress(&address, ekv_static_staging_ring),
+                            "look up the built-in staging ring");
+            ekv::require(address != nullptr, "built-in staging ring has no device address");
+            g_static_ring_address[device] = address;
+        }
+        ring = g_static_ring_address[device];
+    });
+    if (status) return status;
+    return ekv::staged_impl(planes, n_planes, row_bytes, plane_index, slots, slots_esize, n_slots, segments,
+                            n_segments, host_staging, n_tasks, ring, kStaticRingBytes, 1, device, stream,
+                            copy_stream);
+}

@@ -193,6 +193,25 @@ int ekv_unpack_rows_staged(
     int device, void* stream, void* copy_stream);
 
 /*
+ * Staged demotion that allocates nothing.  No counterpart in the reference.
+ * Same arguments and result as ekv_pack_rows_staged without `scratch`: the
+ * ring is the library's own 8 MiB device array (4 slots of 2 MiB), held by
+ * every GPU that loads the library until the process exits.  For callers that
+ * cannot allocate device memory when they demote (an engine that reserved all
+ * of HBM for its KV pool, a host without a device allocator).  Rows must be at
+ * most 2 MiB (larger ones are rejected with an error).  The first call on a
+ * device looks up the ring's address with that device current: make it before
+ * any stream capture.  Calls share the ring: calls that overlap on the GPU
+ * race.  Calls no cudaMalloc / cudaFree.
+ */
+int ekv_pack_rows_staged_noalloc(
+    const uint64_t* planes, int n_planes, int64_t row_bytes,
+    const int32_t* plane_index, const void* slots, int slots_esize, int64_t n_slots,
+    const int64_t* segments, int64_t n_segments,
+    void* host_staging, int64_t n_tasks,
+    int device, void* stream, void* copy_stream);
+
+/*
  * R4/R6 — page -> chunk projection counts.  Restates PhysicalPages.chunks
  * (adaptive_sparse/minimax_vmm.py:40-52) and _chunk_release_counts
  * (adaptive_sparse/scheduler_budget.py:155-156): for each page and plane p,
