@@ -159,6 +159,49 @@ __device__ __forceinline__ void copy_row_any(const GatherParams& p, bool valid, 
     }
 }
 
+// Copy of a whole batch of rows (row k of the batch is row0 + k * warps, its
+// byte offset in lane k's `mine`) when a row is small: the (row, plane, vector)
+// space is flattened so that the kUnroll vectors each lane keeps in flight span
+// several rows.  Every address must be 16-byte aligned.
+constexpr uint32_t kFlatRowLimit = 32 * kUnroll;  // vectors per row (all planes) below which to flatten
+
+__device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t mine, int64_t row0,
+                                                 int64_t warps, int nb, unsigned lane) {
+    const uint32_t vecs = static_cast<uint32_t>(p.row_bytes >> 4);
+    const uint32_t per_row = static_cast<uint32_t>(p.n_planes) * vecs;
+    const uint32_t total = static_cast<uint32_t>(nb) * per_row;
+    for (uint32_t base = 0; base < total; base += 32 * kUnroll) {
+        uint4 v[kUnroll];
+        uint32_t row_of[kUnroll];
+        uint32_t rem_of[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t idx = base + u * 32 + lane;
+            const uint32_t k = idx < total ? idx / per_row : 0;
+            const int64_t s = __shfl_sync(0xffffffffu, mine, static_cast<int>(k));
+            const uint32_t rem = idx - k * per_row;
+            row_of[u] = k;
+            rem_of[u] = rem;
+            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (idx < total && s >= 0) {
+                const uint32_t plane = p.vec_shift >= 0 ? (rem >> p.vec_shift) : rem / vecs;
+                const uint32_t vec = rem - plane * vecs;
+                v[u] = load_vec(reinterpret_cast<const uint4*>(p.src[plane] + s) + vec);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t idx = base + u * 32 + lane;
+            if (idx < total) {
+                const uint32_t plane = p.vec_shift >= 0 ? (rem_of[u] >> p.vec_shift) : rem_of[u] / vecs;
+                const uint32_t vec = rem_of[u] - plane * vecs;
+                char* row = p.dst[plane] + (row0 + static_cast<int64_t>(row_of[u]) * warps) * p.row_bytes;
+                store_vec(reinterpret_cast<uint4*>(row) + vec, v[u]);
+            }
+        }
+    }
+}
+
 // Rows are taken 32 at a time per warp (row0 + k * warps, k < 32): every lane
 // resolves one row's index chain, so the three dependent index loads are paid
 // once per 32 rows instead of once per row; the warp then streams each row out
@@ -185,6 +228,12 @@ gather_kernel(const __grid_constant__ GatherParams p) {
         const int64_t mine = valid ? src : -1;
         const int64_t left = (n_rows - row0 + warps - 1) / warps;
         const int nb = static_cast<int>(left < 32 ? left : 32);
+        const bool small_rows = p.row_bytes % 16 == 0 && p.plane_or % 16 == 0 &&
+                                static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) <= kFlatRowLimit;
+        if (small_rows && !__ballot_sync(0xffffffffu, valid && (src & 15))) {
+            copy_batch_vec16(p, mine, row0, warps, nb, lane);
+            continue;
+        }
         for (int k = 0; k < nb; ++k) {
             const int64_t s = __shfl_sync(0xffffffffu, mine, k);
             copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane);

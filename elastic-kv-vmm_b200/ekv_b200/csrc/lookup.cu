@@ -102,10 +102,14 @@ struct LookupParams {
 
 constexpr int kLookupThreads = 512;
 constexpr int kLookupWarps = kLookupThreads / 32;
+constexpr int kLookupItems = 4;                             // consecutive columns per thread
+constexpr int kLookupTile = kLookupThreads * kLookupItems;  // columns per pass (2048)
 
-// One block per request row; each pass covers kLookupThreads Top-K columns.
-// Misses are compacted in column order: a warp ballot ranks lanes inside the
-// warp, a shared-memory scan of the warp totals ranks warps inside the pass.
+// One block per request row; a pass covers kLookupTile Top-K columns, each
+// thread kLookupItems consecutive ones, so a 2048-wide row is one pass with all
+// its independent map lookups in flight at once.  Misses are compacted in
+// column order by a block-wide exclusive scan of the per-thread miss counts
+// (warp shuffle scan, then a scan of the warp totals in shared memory).
 __global__ void __launch_bounds__(kLookupThreads)
 lookup_kernel(const __grid_constant__ LookupParams p) {
     __shared__ int warp_totals[kLookupWarps];
@@ -118,33 +122,55 @@ lookup_kernel(const __grid_constant__ LookupParams p) {
             limit = length < limit ? length : limit;
         }
         int64_t base = 0;
-        for (int64_t c0 = 0; c0 < p.k; c0 += kLookupThreads) {
-            const int64_t i = c0 + threadIdx.x;
-            const bool active = i < p.k;
-            int64_t token = -1;
-            int64_t slot = -1;
-            if (active) token = load_index(p.topk, p.topk_es, b * p.topk_row + i);
-            const bool valid = active && token >= 0 && token < limit;
-            if (valid) slot = load_index(p.map, p.map_es, b * p.map_row + token);
-            const bool is_miss = valid && slot < 0;
-            if (active) {
-                p.slots[b * p.slots_row + i] = static_cast<int32_t>(slot);
-                if (p.miss) p.miss[b * p.miss_row + i] = is_miss ? 1 : 0;
+        for (int64_t c0 = 0; c0 < p.k; c0 += kLookupTile) {
+            const int64_t first = c0 + static_cast<int64_t>(threadIdx.x) * kLookupItems;
+            int64_t token[kLookupItems];
+            int64_t slot[kLookupItems];
+#pragma unroll
+            for (int j = 0; j < kLookupItems; ++j) {
+                token[j] = first + j < p.k ? load_index(p.topk, p.topk_es, b * p.topk_row + first + j) : -1;
             }
-            const unsigned ballot = __ballot_sync(0xffffffffu, is_miss);
-            if (lane == 0) warp_totals[warp] = __popc(ballot);
+            int count = 0;
+            unsigned miss_bits = 0;
+#pragma unroll
+            for (int j = 0; j < kLookupItems; ++j) {
+                const bool valid = token[j] >= 0 && token[j] < limit;
+                slot[j] = valid ? load_index(p.map, p.map_es, b * p.map_row + token[j]) : -1;
+                if (valid && slot[j] < 0) {
+                    miss_bits |= 1u << j;
+                    ++count;
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kLookupItems; ++j) {
+                if (first + j < p.k) {
+                    p.slots[b * p.slots_row + first + j] = static_cast<int32_t>(slot[j]);
+                    if (p.miss) p.miss[b * p.miss_row + first + j] = (miss_bits >> j) & 1u;
+                }
+            }
+            // Exclusive prefix of `count` over the block, in thread (= column) order.
+            int inclusive = count;
+#pragma unroll
+            for (int offset = 1; offset < 32; offset <<= 1) {
+                const int other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+                if (lane >= static_cast<unsigned>(offset)) inclusive += other;
+            }
+            if (lane == 31) warp_totals[warp] = inclusive;
             __syncthreads();
             int before = 0;
             int total = 0;
 #pragma unroll
             for (int w = 0; w < kLookupWarps; ++w) {
-                const int count = warp_totals[w];
-                before += w < warp ? count : 0;
-                total += count;
+                const int warp_count = warp_totals[w];
+                before += w < warp ? warp_count : 0;
+                total += warp_count;
             }
-            if (is_miss && p.miss_list) {
-                const int rank = __popc(ballot & ((1u << lane) - 1u));
-                p.miss_list[b * p.list_row + base + before + rank] = static_cast<int32_t>(token);
+            if (miss_bits && p.miss_list) {
+                int64_t at = base + before + inclusive - count;
+#pragma unroll
+                for (int j = 0; j < kLookupItems; ++j) {
+                    if ((miss_bits >> j) & 1u) p.miss_list[b * p.list_row + at++] = static_cast<int32_t>(token[j]);
+                }
             }
             base += total;
             __syncthreads();  // warp_totals is rewritten by the next pass

@@ -52,6 +52,43 @@ def resolve_resident(topk, table, mapping, rows, lengths, selected, output, bloc
     )
 
 
+class LookupPlan:
+    """``lookup_slots`` pre-bound to fixed tensors for a hot loop (or a CUDA graph).
+
+    Each call only launches; the tensors must outlive the plan and keep their
+    storage.  ``slots``, ``miss``, ``miss_list`` and ``miss_count`` hold the
+    results after every call.
+    """
+
+    def __init__(self, residency_map, topk, lengths=None, *, slots=None, miss=None, miss_list=None,
+                 miss_count=None):
+        device = require_cuda(dict(residency_map=residency_map, topk=topk, lengths=lengths))
+        batch, k = topk.shape
+        self.slots = slots if slots is not None else torch.empty((batch, k), dtype=torch.int32, device=device)
+        self.miss = miss if miss is not None else torch.empty((batch, k), dtype=torch.bool, device=device)
+        self.miss_list = (miss_list if miss_list is not None
+                          else torch.empty((batch, k), dtype=torch.int32, device=device))
+        self.miss_count = (miss_count if miss_count is not None
+                           else torch.empty((batch,), dtype=torch.int32, device=device))
+        # Validate once through the public function (this also runs the lookup).
+        lookup_slots(residency_map, topk, lengths, slots=self.slots, miss=self.miss,
+                     miss_list=self.miss_list, miss_count=self.miss_count)
+        self.device = device
+        self._keep = (residency_map, topk, lengths)
+        self._args = (
+            residency_map.data_ptr(), index_esize(residency_map, "residency_map"),
+            residency_map.stride(0), residency_map.shape[1],
+            topk.data_ptr(), index_esize(topk, "topk"), topk.stride(0),
+            None if lengths is None else lengths.data_ptr(),
+            4 if lengths is None else index_esize(lengths, "lengths"),
+            batch, k, self.slots.data_ptr(), self.slots.stride(0), self.miss.data_ptr(), self.miss.stride(0),
+            self.miss_list.data_ptr(), self.miss_list.stride(0), self.miss_count.data_ptr(), device.index,
+        )
+
+    def __call__(self, stream: int | None = None) -> None:
+        call("ekv_lookup_slots", *self._args, stream_handle(self.device) if stream is None else stream)
+
+
 def lookup_slots(residency_map, topk, lengths=None, *, slots=None, miss=None, miss_list=None,
                  miss_count=None, compact=True):
     """Token ids -> hot slots through a per-request residency map.
