@@ -94,6 +94,22 @@ _KERNELS = {
         _p, _i64,
         _i32, _p, _p,
     ],
+    "ekv_swap_select": [
+        _p, _i64, _i64,
+        _p, _i64, _i64,
+        _p,
+        _p, _i64, _i64,
+        _p, _i64, _p,
+        _p, _i64,
+        _i64, _i32, _p,
+    ],
+    "ekv_promote_rows": [
+        _u64p, _u64p, _i32, _i64,
+        _i64, _i64, _i64,
+        _p, _i64, _p,
+        _p, _i64,
+        _i64, _i64, _i32, _p,
+    ],
     "ekv_chunk_counts": [
         _p, _i32, _i64,
         _i64p, _i64p, _i32,

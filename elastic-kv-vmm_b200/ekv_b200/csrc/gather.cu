@@ -74,9 +74,17 @@ __device__ __forceinline__ int64_t resolve_row(const GatherParams& p, int64_t r,
     if (!valid) return 0;
     const int64_t req = load_index(p.request_ids, p.req_es, b);
     int64_t element;
-    if (p.indirect) {
+    if (p.indirect == 1) {
         const int64_t logical = load_index(p.request_table, p.table_es, req * p.table_width + pos);
         element = load_index(p.slot_offsets, p.off_es, logical);
+    } else if (p.indirect == 2) {
+        // Mapped: the table holds the row's slot in the request's fixed region, -1 if absent.
+        const int64_t slot = load_index(p.request_table, p.table_es, req * p.table_width + pos);
+        if (slot < 0) {
+            valid = false;
+            return 0;
+        }
+        element = p.sink_elements + req * p.request_stride + slot * p.width;
     } else {
         element = p.sink_elements + req * p.request_stride + pos * p.width;
     }
@@ -449,10 +457,14 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         check_esize(positions_esize, "positions");
         check_esize(request_ids_esize, "request_ids");
         check_esize(lengths_esize, "lengths");
-        if (indirect) {
+        require(indirect >= 0 && indirect <= 2, "addressing mode must be 0 (direct), 1 (indirect) or 2 (mapped)");
+        if (indirect == 1) {
             require(request_table && slot_offsets, "indirect gather needs request_table and slot_offsets");
             check_esize(table_esize, "request_table");
             check_esize(offsets_esize, "slot_offsets");
+        } else if (indirect == 2) {
+            require(request_table, "mapped gather needs request_table (the residency map)");
+            check_esize(table_esize, "request_table");
         }
         GatherParams p{};
         p.positions = positions;
@@ -472,8 +484,8 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         p.req_es = request_ids_esize;
         p.len_es = lengths_esize;
         p.table_es = indirect ? table_esize : 8;
-        p.off_es = indirect ? offsets_esize : 8;
-        p.indirect = indirect ? 1 : 0;
+        p.off_es = indirect == 1 ? offsets_esize : 8;
+        p.indirect = indirect;
         p.n_planes = n_planes;
         p.vec_shift = (p.row_bytes % 16) ? -1 : log2_exact(p.row_bytes / 16);
         uint64_t plane_or = 0;

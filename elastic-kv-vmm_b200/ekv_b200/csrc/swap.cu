@@ -1,0 +1,296 @@
+// Hot-buffer swap-in: victim selection and promotion copies for Top-K misses.
+//
+// The reference hands sparse-attention misses to SGLang's block swap kernel
+// (hisparse.cuh, called from adaptive_sparse/request_residency.py:805-809 and
+// :829-832): rows missing from a request's fixed hot buffer are loaded from the
+// host KV pool into evicted hot slots, least recently used first.  Here the same
+// job is split into two device-driven steps so that a decode step needs no host
+// round trip (and can be replayed from a CUDA graph):
+//
+//   swap_select  one block per request.  Hot slots referenced by this step's
+//                hits are marked in a shared-memory bitmap; the request's misses
+//                (the compacted miss list of the lookup) take the first
+//                unreferenced slots in clock order from the request's hand, found
+//                with a block-wide ordered scan.  The residency map and the
+//                slot -> token table are updated (evicted token -> -1, missed
+//                token -> its new slot) and the hand moves past the last victim.
+//   promote      a persistent grid copies every miss's row, in every plane of
+//                the layer, from host history (pinned memory read through
+//                unified addressing, or device memory) into its new hot slot of
+//                the fixed-position hot pool (sink chunk, then one region per
+//                request); tasks beyond a request's miss count are skipped.
+//
+// Victim choice (clock order, hits pinned) is this build's policy; the
+// reference's LRU lives in third-party code that is not part of the reference.
+#include "common.cuh"
+
+namespace ekv {
+namespace {
+
+struct SelectParams {
+    int32_t* res_map;
+    int32_t* slot_token;
+    int32_t* hand;
+    const int32_t* slots;
+    const int32_t* miss_list;
+    const int32_t* miss_count;
+    int32_t* promo_slot;
+    int64_t map_row, map_width, token_row, hot, slots_row, k, list_row, promo_row, batch;
+};
+
+constexpr int kSelectThreads = 512;
+constexpr int kSelectWarps = kSelectThreads / 32;
+constexpr int kSelectItems = 4;
+constexpr int kMaxHot = 1 << 16;  // shared bitmap: 8 KiB
+
+__global__ void __launch_bounds__(kSelectThreads)
+swap_select_kernel(const __grid_constant__ SelectParams p) {
+    __shared__ uint32_t referenced[kMaxHot / 32];
+    __shared__ int warp_totals[kSelectWarps];
+    __shared__ int found_total;
+    const unsigned lane = lane_id();
+    const int warp = threadIdx.x >> 5;
+    const int words = static_cast<int>((p.hot + 31) / 32);
+    for (int64_t b = blockIdx.x; b < p.batch; b += gridDim.x) {
+        for (int w = threadIdx.x; w < words; w += kSelectThreads) referenced[w] = 0u;
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < p.k; i += kSelectThreads) {
+            const int32_t s = p.slots[b * p.slots_row + i];
+            if (s >= 0 && s < p.hot) atomicOr(&referenced[s >> 5], 1u << (s & 31));
+        }
+        __syncthreads();
+        const int64_t misses = p.miss_count[b];
+        const int64_t start = ((static_cast<int64_t>(p.hand[b]) % p.hot) + p.hot) % p.hot;
+        for (int64_t r = threadIdx.x; r < p.k; r += kSelectThreads) p.promo_slot[b * p.promo_row + r] = -1;
+        __syncthreads();
+        // Walk the ring from the hand in tiles; rank the free (unreferenced)
+        // slots in ring order and give rank r to miss r.
+        int64_t taken = 0;
+        for (int64_t j0 = 0; j0 < p.hot && taken < misses; j0 += kSelectThreads * kSelectItems) {
+            const int64_t first = j0 + static_cast<int64_t>(threadIdx.x) * kSelectItems;
+            int64_t slot[kSelectItems];
+            unsigned free_bits = 0;
+            int count = 0;
+#pragma unroll
+            for (int j = 0; j < kSelectItems; ++j) {
+                slot[j] = -1;
+                if (first + j < p.hot) {
+                    int64_t s = start + first + j;
+                    if (s >= p.hot) s -= p.hot;
+                    slot[j] = s;
+                    if (!((referenced[s >> 5] >> (s & 31)) & 1u)) {
+                        free_bits |= 1u << j;
+                        ++count;
+                    }
+                }
+            }
+            int inclusive = count;
+#pragma unroll
+            for (int offset = 1; offset < 32; offset <<= 1) {
+                const int other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+                if (lane >= static_cast<unsigned>(offset)) inclusive += other;
+            }
+            if (lane == 31) warp_totals[warp] = inclusive;
+            __syncthreads();
+            int before = 0, total = 0;
+#pragma unroll
+            for (int w = 0; w < kSelectWarps; ++w) {
+                before += w < warp ? warp_totals[w] : 0;
+                total += warp_totals[w];
+            }
+            int64_t rank = taken + before + inclusive - count;
+#pragma unroll
+            for (int j = 0; j < kSelectItems; ++j) {
+                if ((free_bits >> j) & 1u) {
+                    if (rank < misses) {
+                        p.promo_slot[b * p.promo_row + rank] = static_cast<int32_t>(slot[j]);
+                        if (rank == misses - 1) {
+                            const int64_t next = slot[j] + 1;
+                            p.hand[b] = static_cast<int32_t>(next == p.hot ? 0 : next);
+                        }
+                    }
+                    ++rank;
+                }
+            }
+            taken += total;
+            __syncthreads();  // warp_totals reused; promo_slot visible below
+        }
+        if (threadIdx.x == 0) found_total = static_cast<int>(taken < misses ? taken : misses);
+        __syncthreads();
+        const int64_t assigned = found_total;
+        // Publish: evicted tokens leave the map, missed tokens enter it.  Every
+        // victim holds a distinct resident token and no miss is resident, so the
+        // writes never collide.
+        for (int64_t r = threadIdx.x; r < assigned; r += kSelectThreads) {
+            const int32_t v = p.promo_slot[b * p.promo_row + r];
+            const int32_t token = p.miss_list[b * p.list_row + r];
+            const int32_t old = p.slot_token[b * p.token_row + v];
+            if (old >= 0 && old < p.map_width) p.res_map[b * p.map_row + old] = -1;
+            if (token >= 0 && token < p.map_width) p.res_map[b * p.map_row + token] = v;
+            p.slot_token[b * p.token_row + v] = token;
+        }
+        __syncthreads();
+    }
+}
+
+struct PromoteParams {
+    const int32_t* miss_list;
+    const int32_t* miss_count;
+    const int32_t* promo_slot;
+    int64_t list_row, promo_row, batch, k;
+    int64_t row_bytes, history_rows_per_request, sink_bytes, request_bytes;
+    uint64_t addr_or;
+    int n_planes;
+    const char* history[EKV_MAX_PLANES];
+    char* hot[EKV_MAX_PLANES];
+};
+
+constexpr int kPromoteThreads = 256;
+constexpr int kPromoteWarps = kPromoteThreads / 32;
+
+template <typename T>
+__device__ __forceinline__ void warp_move(const char* src, char* dst, int64_t bytes, unsigned lane) {
+    const int64_t n = bytes / static_cast<int64_t>(sizeof(T));
+    const T* s = reinterpret_cast<const T*>(src);
+    T* d = reinterpret_cast<T*>(dst);
+    for (int64_t base = 0; base < n; base += 32 * 4) {
+        T v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t e = base + u * 32 + lane;
+            if (e < n) v[u] = s[e];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t e = base + u * 32 + lane;
+            if (e < n) d[e] = v[u];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kPromoteThreads)
+promote_kernel(const __grid_constant__ PromoteParams p) {
+    const int64_t tasks = p.batch * p.k * p.n_planes;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kPromoteWarps;
+    const unsigned lane = lane_id();
+    // Task order: plane fastest, so consecutive warps move one miss's K and V.
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kPromoteWarps + (threadIdx.x >> 5); t < tasks;
+         t += warps) {
+        const int64_t plane = t % p.n_planes;
+        const int64_t item = t / p.n_planes;
+        const int64_t b = item / p.k;
+        const int64_t r = item - b * p.k;
+        if (r >= p.miss_count[b]) continue;
+        const int32_t slot = p.promo_slot[b * p.promo_row + r];
+        const int32_t token = p.miss_list[b * p.list_row + r];
+        if (slot < 0 || token < 0 || token >= p.history_rows_per_request) continue;
+        const char* src = p.history[plane] + (b * p.history_rows_per_request + token) * p.row_bytes;
+        char* dst = p.hot[plane] + p.sink_bytes + b * p.request_bytes + static_cast<int64_t>(slot) * p.row_bytes;
+        const int64_t align = alignment_of(p.addr_or | static_cast<uint64_t>(p.row_bytes));
+        if (align == 16) {
+            warp_move<uint4>(src, dst, p.row_bytes, lane);
+        } else {
+            warp_move<uint8_t>(src, dst, p.row_bytes, lane);
+        }
+    }
+}
+
+}  // namespace
+}  // namespace ekv
+
+using namespace ekv;
+
+extern "C" int ekv_swap_select(
+    int32_t* res_map, int64_t map_row_stride, int64_t map_width,
+    int32_t* slot_token, int64_t token_row_stride, int64_t hot_capacity,
+    int32_t* hand,
+    const int32_t* slots, int64_t slots_row_stride, int64_t k,
+    const int32_t* miss_list, int64_t list_row_stride, const int32_t* miss_count,
+    int32_t* promo_slot, int64_t promo_row_stride,
+    int64_t batch, int device, void* stream) {
+    return guarded([&] {
+        require(batch >= 0 && k >= 0 && map_width >= 0, "sizes must be non-negative");
+        require(hot_capacity > 0 && hot_capacity <= kMaxHot, "hot capacity outside [1, 65536]");
+        if (!batch || !k) return;
+        require(res_map && slot_token && hand && slots && miss_list && miss_count && promo_slot,
+                "null pointer argument");
+        bind_device(device);
+        SelectParams p{};
+        p.res_map = res_map;
+        p.slot_token = slot_token;
+        p.hand = hand;
+        p.slots = slots;
+        p.miss_list = miss_list;
+        p.miss_count = miss_count;
+        p.promo_slot = promo_slot;
+        p.map_row = map_row_stride;
+        p.map_width = map_width;
+        p.token_row = token_row_stride;
+        p.hot = hot_capacity;
+        p.slots_row = slots_row_stride;
+        p.k = k;
+        p.list_row = list_row_stride;
+        p.promo_row = promo_row_stride;
+        p.batch = batch;
+        const unsigned grid = static_cast<unsigned>(batch < (1 << 20) ? batch : (1 << 20));
+        swap_select_kernel<<<grid, kSelectThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        check_launch("swap_select launch");
+    });
+}
+
+extern "C" int ekv_promote_rows(
+    const uint64_t* history_planes, const uint64_t* hot_planes, int n_planes, int64_t row_bytes,
+    int64_t history_rows_per_request, int64_t sink_bytes, int64_t request_bytes,
+    const int32_t* miss_list, int64_t list_row_stride, const int32_t* miss_count,
+    const int32_t* promo_slot, int64_t promo_row_stride,
+    int64_t batch, int64_t k, int device, void* stream) {
+    return guarded([&] {
+        require(batch >= 0 && k >= 0, "sizes must be non-negative");
+        require(row_bytes > 0 && history_rows_per_request > 0, "row and history sizes must be positive");
+        require(n_planes >= 1 && n_planes <= EKV_MAX_PLANES, "plane count outside [1, EKV_MAX_PLANES]");
+        if (!batch || !k) return;
+        require(history_planes && hot_planes && miss_list && miss_count && promo_slot, "null pointer argument");
+        bind_device(device);
+        PromoteParams p{};
+        p.miss_list = miss_list;
+        p.miss_count = miss_count;
+        p.promo_slot = promo_slot;
+        p.list_row = list_row_stride;
+        p.promo_row = promo_row_stride;
+        p.batch = batch;
+        p.k = k;
+        p.row_bytes = row_bytes;
+        p.history_rows_per_request = history_rows_per_request;
+        p.sink_bytes = sink_bytes;
+        p.request_bytes = request_bytes;
+        p.n_planes = n_planes;
+        uint64_t addr_or = static_cast<uint64_t>(sink_bytes) | static_cast<uint64_t>(request_bytes);
+        for (int i = 0; i < n_planes; ++i) {
+            require(history_planes[i] && hot_planes[i], "null plane address");
+            // History may live in pinned host memory: use its device view, refuse anything unmapped.
+            cudaPointerAttributes attr{};
+            cuda_check(cudaPointerGetAttributes(&attr, reinterpret_cast<const void*>(history_planes[i])),
+                       "query history pointer");
+            const void* view = reinterpret_cast<const void*>(history_planes[i]);
+            if (attr.type == cudaMemoryTypeHost) {
+                require(attr.devicePointer != nullptr, "pinned history is not mapped for device access");
+                view = attr.devicePointer;
+            } else {
+                require(attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged,
+                        "history must be device memory or pinned host memory");
+            }
+            p.history[i] = static_cast<const char*>(view);
+            p.hot[i] = reinterpret_cast<char*>(hot_planes[i]);
+            addr_or |= reinterpret_cast<uint64_t>(view) | hot_planes[i];
+        }
+        p.addr_or = addr_or;
+        static int cached[64] = {0};
+        int grid = device < 64 ? cached[device] : 0;
+        if (!grid) {
+            grid = persistent_grid(reinterpret_cast<const void*>(promote_kernel), kPromoteThreads, 0, device);
+            if (device < 64) cached[device] = grid;
+        }
+        promote_kernel<<<grid, kPromoteThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        check_launch("promote_rows launch");
+    });
+}

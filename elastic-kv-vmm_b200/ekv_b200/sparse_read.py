@@ -12,11 +12,20 @@ from __future__ import annotations
 from ._lib import MAX_PLANES, call, index_esize, require_cuda, stream_handle, u64_array
 
 
-def _index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect):
-    if indirect and (request_table is None or slot_offsets is None):
+def _mode(indirect, mapped):
+    """Addressing mode of the C ABI: 0 direct, 1 indirect (software table), 2 mapped."""
+    if mapped and indirect:
+        raise ValueError("choose indirect or mapped addressing, not both")
+    return 2 if mapped else int(bool(indirect))
+
+
+def _index_args(positions, request_ids, lengths, request_table, slot_offsets, mode):
+    if mode == 1 and (request_table is None or slot_offsets is None):
         raise ValueError("indirect gather needs request_table and slot_offsets")
-    table = request_table if indirect else None
-    offsets = slot_offsets if indirect else None
+    if mode == 2 and request_table is None:
+        raise ValueError("mapped gather needs request_table (the residency map)")
+    table = request_table if mode else None
+    offsets = slot_offsets if mode == 1 else None
     return (
         positions.data_ptr(), index_esize(positions, "positions"),
         request_ids.data_ptr(), index_esize(request_ids, "request_ids"),
@@ -60,7 +69,7 @@ def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offset
     call(
         "ekv_gather_rows",
         raw.data_ptr(), output.data_ptr(), raw.element_size(),
-        *_index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect),
+        *_index_args(positions, request_ids, lengths, request_table, slot_offsets, int(bool(indirect))),
         batch, selected, layout.row_elements,
         layout.max_tokens, layout.request_bytes // layout.itemsize,
         layout.chunk_bytes // layout.itemsize,
@@ -69,13 +78,19 @@ def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offset
 
 
 def gather_rows_planes(planes, positions, request_ids, lengths, request_table, slot_offsets,
-                       outputs, layout, *, indirect):
+                       outputs, layout, *, indirect, mapped=False):
     """``gather_rows`` over every plane in ``planes`` with one row selection.
 
     ``planes[p]`` and ``outputs[p]`` play the roles of ``raw`` and ``output``
     for plane p (e.g. layer l's K at p = 2l and V at p = 2l + 1).  Element
     offsets are relative to each plane's start.  Planes are processed
     EKV_MAX_PLANES per launch.
+
+    ``mapped=True`` (new, beside the reference's two modes) reads
+    ``request_table`` as a residency map: ``s = request_table[req, pos]`` is the
+    row's slot in the request's fixed region (``sink + req * request_stride +
+    s * width``), and ``s < 0`` reads as a zero row -- a lookup and its gather
+    in one launch.
     """
     planes = list(planes)
     outputs = list(outputs)
@@ -98,7 +113,10 @@ def gather_rows_planes(planes, positions, request_ids, lengths, request_table, s
             raise ValueError("planes and outputs must be contiguous")
         if plane.dtype != output.dtype or plane.element_size() != itemsize:
             raise TypeError("all planes and outputs must share one dtype")
-    args = _index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect)
+    mode = _mode(indirect, mapped)
+    args = _index_args(positions, request_ids, lengths, request_table, slot_offsets, mode)
+    # A residency map is indexed by token: its row width is the map's, not the layout's.
+    table_width = request_table.shape[-1] if mode == 2 else layout.max_tokens
     stream = stream_handle(device)
     for start in range(0, len(planes), MAX_PLANES):
         src = planes[start:start + MAX_PLANES]
@@ -107,9 +125,9 @@ def gather_rows_planes(planes, positions, request_ids, lengths, request_table, s
             "ekv_gather_rows_planes",
             u64_array(t.data_ptr() for t in src), u64_array(t.data_ptr() for t in dst), len(src),
             itemsize, *args, batch, selected, layout.row_elements,
-            layout.max_tokens, layout.request_bytes // layout.itemsize,
+            table_width, layout.request_bytes // layout.itemsize,
             layout.chunk_bytes // layout.itemsize,
-            int(bool(indirect)), device.index, stream,
+            mode, device.index, stream,
         )
 
 
@@ -121,7 +139,7 @@ class PlaneGather:
     """
 
     def __init__(self, planes, positions, request_ids, lengths, request_table, slot_offsets,
-                 outputs, layout, *, indirect):
+                 outputs, layout, *, indirect, mapped=False):
         planes = list(planes)
         outputs = list(outputs)
         if not planes or len(planes) != len(outputs) or len(planes) > MAX_PLANES:
@@ -143,12 +161,15 @@ class PlaneGather:
         self._keep = (planes, outputs, index)
         self._src = u64_array(t.data_ptr() for t in planes)
         self._dst = u64_array(t.data_ptr() for t in outputs)
+        mode = _mode(indirect, mapped)
+        # A residency map is indexed by token: its row width is the map's, not the layout's.
+        table_width = request_table.shape[-1] if mode == 2 else layout.max_tokens
         self._args = (
             self._src, self._dst, len(planes), planes[0].element_size(),
-            *_index_args(positions, request_ids, lengths, request_table, slot_offsets, indirect),
+            *_index_args(positions, request_ids, lengths, request_table, slot_offsets, mode),
             batch, selected, layout.row_elements,
-            layout.max_tokens, layout.request_bytes // layout.itemsize,
-            layout.chunk_bytes // layout.itemsize, int(bool(indirect)), self.device.index,
+            table_width, layout.request_bytes // layout.itemsize,
+            layout.chunk_bytes // layout.itemsize, _mode(indirect, mapped), self.device.index,
         )
         self.empty = not batch or not selected
 

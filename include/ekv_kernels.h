@@ -93,9 +93,14 @@ int ekv_lookup_slots(
  * (experimental/sparse_read.py:11-51).  For b < batch, i < selected:
  *     pos = positions[b*selected + i], req = request_ids[b]
  *     valid = 0 <= pos < lengths[b]
- *     off = indirect ? slot_offsets[request_table[req*table_width + pos]]
- *                    : sink_elements + req*request_stride + pos*width
+ *     off = indirect == 1 ? slot_offsets[request_table[req*table_width + pos]]
+ *         : indirect == 2 ? sink_elements + req*request_stride + s*width
+ *                           with s = request_table[req*table_width + pos]  (valid only if s >= 0)
+ *         :                 sink_elements + req*request_stride + pos*width
  *     out[(b*selected + i)*width + c] = valid ? raw[off + c] : 0,  c < width
+ * Modes 0 and 1 are the reference's direct and software-table addressing; mode
+ * 2 ("mapped", new) reads a residency map (token -> slot in the request's fixed
+ * region, -1 = absent) so a lookup and its gather are one launch.
  * Offsets, strides and width are counted in elements of `itemsize` bytes; the
  * payload is copied bit for bit.  Index arrays are contiguous.
  */
@@ -210,6 +215,43 @@ int ekv_pack_rows_staged_noalloc(
     const int64_t* segments, int64_t n_segments,
     void* host_staging, int64_t n_tasks,
     int device, void* stream, void* copy_stream);
+
+/*
+ * Hot-buffer swap-in, step 1: victim selection.  Replaces the LRU half of the
+ * block swap kernel the reference calls through SGLang's coordinator
+ * (adaptive_sparse/request_residency.py:805-809, :829-832).  One block per row b:
+ * hot slots referenced by this step's hits (slots[b, :] >= 0, from
+ * ekv_lookup_slots) are pinned; misses r < miss_count[b] (miss_list[b, r]) take
+ * the first unreferenced slots in ring order starting at hand[b], written to
+ * promo_slot[b, r] (-1 for r >= the number assigned); then
+ * res_map[b, evicted token] = -1, res_map[b, miss token] = slot,
+ * slot_token[b, slot] = miss token, hand[b] = last victim + 1 (mod hot_capacity).
+ * All arrays int32; hot_capacity <= 65536.  Top-K token ids must be unique per row.
+ */
+int ekv_swap_select(
+    int32_t* res_map, int64_t map_row_stride, int64_t map_width,
+    int32_t* slot_token, int64_t token_row_stride, int64_t hot_capacity,
+    int32_t* hand,
+    const int32_t* slots, int64_t slots_row_stride, int64_t k,
+    const int32_t* miss_list, int64_t list_row_stride, const int32_t* miss_count,
+    int32_t* promo_slot, int64_t promo_row_stride,
+    int64_t batch, int device, void* stream);
+
+/*
+ * Hot-buffer swap-in, step 2: promotion copies.  Replaces the host -> hot-buffer
+ * loads of the same swap kernel.  For every row b, r < miss_count[b] with
+ * promo_slot[b, r] = s >= 0 and token t = miss_list[b, r], and every plane p:
+ *     hot_planes[p] + sink_bytes + b*request_bytes + s*row_bytes
+ *         <- history_planes[p] + (b*history_rows_per_request + t)*row_bytes
+ * history_planes may be pinned host memory (read through unified addressing)
+ * or device memory; both plane arrays are HOST arrays of n_planes addresses.
+ */
+int ekv_promote_rows(
+    const uint64_t* history_planes, const uint64_t* hot_planes, int n_planes, int64_t row_bytes,
+    int64_t history_rows_per_request, int64_t sink_bytes, int64_t request_bytes,
+    const int32_t* miss_list, int64_t list_row_stride, const int32_t* miss_count,
+    const int32_t* promo_slot, int64_t promo_row_stride,
+    int64_t batch, int64_t k, int device, void* stream);
 
 /*
  * R4/R6 — page -> chunk projection counts.  Restates PhysicalPages.chunks
