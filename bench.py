@@ -54,8 +54,9 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--config", type=int, choices=(2, 4), default=2,
-                   help="2 = headline gather (default); 4 = TP-sharded lookup + gather + bitmap combine")
+    p.add_argument("--config", type=int, choices=(2, 4, 5), default=2,
+                   help="2 = headline gather (default); 4 = TP-sharded lookup + gather + bitmap combine; "
+                        "5 = multi-step decode with swap-in from host history")
     p.add_argument("--layers", type=int, default=None,
                    help="layers (default: 36 for config 2, 48 for config 4; fewer only for profiling captures)")
     p.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -747,6 +748,188 @@ def run_config4(args, dist: Dist):
     return result
 
 
+CFG5 = dict(layers=48, kv_heads=8, head_dim=128, requests=128, context=65536, hot=8192, topk=2048, steps=64,
+            keep=0.9, zipf_s=1.1)
+
+
+def zipf_topk_schedule(steps, batch, context, k, keep, s, seed):
+    """Top-K token ids per decode step [steps, batch, k] (int32, distinct per row).
+
+    Step 0 draws k distinct ids; every later step keeps ``keep`` of the previous
+    step's ids and draws the rest from Zipf(s) over the distance from the newest
+    token (distance d -> position context - 1 - d, truncated to the context).
+    """
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+
+    def fresh(row_exclude, n):
+        out = []
+        seen = set(row_exclude)
+        while len(out) < n:
+            d = rng.zipf(s, 4 * (n - len(out)) + 16) - 1
+            for pos in (context - 1 - d[d < context]).tolist():
+                if pos not in seen:
+                    seen.add(pos)
+                    out.append(pos)
+                    if len(out) == n:
+                        break
+        return out
+
+    sched = np.empty((steps, batch, k), dtype=np.int32)
+    n_keep = int(k * keep)
+    for b in range(batch):
+        sched[0, b] = rng.permutation(fresh((), k))
+    for t in range(1, steps):
+        for b in range(batch):
+            kept = sched[t - 1, b, :n_keep].tolist()
+            sched[t, b] = rng.permutation(np.array(kept + fresh(kept, k - n_keep), dtype=np.int32))
+    return sched
+
+
+def run_config5(args, dist: Dist):
+    """Config 5: multi-step sparse decode with host-backed history.  Each step, for every
+    layer: lookup of the step's Top-K in the layer's hot buffer, clock victim selection for
+    the misses, promotion of the missed rows from pinned host history, mapped gather of all
+    Top-K rows -- four launches per layer, replayed from one CUDA graph; the step's Top-K
+    ids are copied from pinned host memory first."""
+    from ekv_b200.host_pool import pinned_buffer
+    from ekv_b200.swap import HotLayer, SwapStep
+
+    c = CFG5
+    dev = dist.device
+    shard = args.tp_shard or dist.world
+    heads = c["kv_heads"] // shard
+    width = heads * c["head_dim"]
+    row_bytes = width * 2
+    batch, ctx, hot, k = c["requests"], c["context"], c["hot"], c["topk"]
+    # 1 GPU without head sharding cannot hold 48 layers of hot buffers (4 GiB per layer).
+    layers = args.layers or (c["layers"] if shard > 1 else 24)
+    steps = args.steps if args.steps != 100 else c["steps"]
+    # Host history shared by every layer (per-layer history would be 1.5 TiB):
+    # word w of token t of request b, plane p = ((b*ctx + t) * words + w) XOR key[p].
+    words = row_bytes // 4
+    keys = [0x5BD1E995, 0x27D4EB2F]
+    history = []
+    rows_total = batch * ctx
+    chunk_rows = max(1, (1 << 30) // row_bytes)
+    for key in keys:
+        host = pinned_buffer(rows_total * row_bytes)[: rows_total * row_bytes].view(rows_total, row_bytes)
+        for r0 in range(0, rows_total, chunk_rows):
+            r1 = min(rows_total, r0 + chunk_rows)
+            vals = (torch.arange(r0 * words, r1 * words, dtype=torch.int64, device=dev) ^ key).to(torch.int32)
+            host[r0:r1].copy_(vals.view(torch.uint8).view(r1 - r0, row_bytes), non_blocking=True)
+        history.append(host)
+    torch.cuda.synchronize()
+    sched = zipf_topk_schedule(steps + 1, batch, ctx, k, c["keep"], c["zipf_s"], seed=55)
+    sched_pinned = torch.from_numpy(sched).pin_memory()
+    topk_dev = torch.empty((batch, k), dtype=torch.int32, device=dev)
+    topk_dev.copy_(sched_pinned[0])
+    hot_layers = [HotLayer(batch, ctx, hot, width, dev) for _ in range(layers)]
+    # One K/V output pair reused by every layer, as a decode step consumes each
+    # layer's rows before the next layer runs.
+    shared_out = [torch.empty((batch, k, width), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    outputs = [shared_out for _ in range(layers)]
+    plans = [SwapStep(layer, topk_dev, [h.view(torch.bfloat16) for h in history], outputs[i])
+             for i, layer in enumerate(hot_layers)]
+    promoted = torch.zeros((), dtype=torch.int64, device=dev)
+
+    def layers_step():
+        for plan in plans:
+            plan()
+            promoted.add_(plan.lookup.miss_count.sum())
+
+    def check(step_ids):
+        """Every gathered row is its token's history row (last layer, both planes)."""
+        ok = True
+        rows = (torch.arange(batch, device=dev)[:, None] * ctx + step_ids.to(torch.int64))
+        w = torch.arange(words, device=dev, dtype=torch.int64)
+        for p, key in enumerate(keys):
+            want = ((rows[..., None] * words + w) ^ key).to(torch.int32)
+            ok &= bool(torch.equal(outputs[-1][p].view(torch.int32).view(batch, k, words), want))
+        return ok
+
+    # Step 0 (cold: every Top-K id misses), timed on its own.
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    layers_step()
+    end.record()
+    end.synchronize()
+    cold_ms = start.elapsed_time(end)
+    cold_promoted = int(promoted.item())
+    parity = check(topk_dev)
+    graph = None
+    capture_error = None
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            topk_dev.copy_(sched_pinned[1], non_blocking=True)
+            layers_step()  # step 1 eagerly (also warms every launch path)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        parity &= check(topk_dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            layers_step()
+    except Exception as exc:
+        graph, capture_error = None, str(exc)
+    promoted.zero_()
+    first = 2
+
+    def step(t):
+        topk_dev.copy_(sched_pinned[t], non_blocking=True)
+        if graph is not None:
+            graph.replay()
+        else:
+            layers_step()
+
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dist.local_rank) as clocks:
+        start.record()
+        for t in range(first, steps + 1):
+            step(t)
+        end.record()
+        end.synchronize()
+    warm_ms = dist.max(start.elapsed_time(end))
+    parity &= check(topk_dev)
+    timed_steps = steps + 1 - first
+    promoted_rows = int(promoted.item())
+    ms_per_step = warm_ms / timed_steps
+    units = batch * k * layers
+    promoted_bytes_step = promoted_rows * 2 * row_bytes / timed_steps
+    gather_bytes_step = units * 4 * row_bytes
+    peak, peak_source = measured_hbm_peak()
+    used_graph = graph is not None
+    del graph
+    return {
+        "metric": METRIC, "value": units / (ms_per_step / 1e3), "unit": "row-pairs/s", "n_gpus": dist.world,
+        "steps": timed_steps, "warmup": first, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded Zipf(1.1) Top-K schedule, 90% kept per step; host history pattern)",
+        "config": {"workload": f"config 5: multi-step sparse decode, {batch} requests x {ctx} context, "
+                               f"{layers} layers, hot {hot}/request, Top-K {k}, lookup -> swap-in -> "
+                               f"promotion from pinned host -> mapped gather per layer",
+                   "layers": layers, "heads_per_rank": heads, "cuda_graph": used_graph,
+                   "capture_error": capture_error,
+                   "cuts": ("host history shared by all layers (per-layer history would be 1.5 TiB); "
+                            + ("24 of 48 layers at 1 GPU (hot buffers are 4 GiB per layer)" if layers < 48 else
+                               "none"))},
+        "cold_step": {"ms": cold_ms, "promoted_rows": cold_promoted,
+                      "promoted_bytes": cold_promoted * 2 * row_bytes},
+        "promoted_rows_per_step": promoted_rows / timed_steps,
+        "promoted_bytes_per_step": promoted_bytes_step,
+        "host_link_gbs": promoted_bytes_step / (ms_per_step / 1e3) / 1e9,
+        "hbm_gbs_per_gpu": (gather_bytes_step + 2 * promoted_bytes_step) / (ms_per_step / 1e3) / 1e9,
+        "hbm_peak": peak, "peak_source": peak_source,
+        "parity_rows_equal_history": bool(parity),
+        "gpu_launches": 4 * layers * timed_steps,
+        "clocks": clocks.summary(),
+    }
+
+
 def run_reference(args, dist: Dist):
     """Reference arm: the torch-CPU restatement on the host cores, rank 0 only."""
     if dist.rank != 0:
@@ -804,7 +987,8 @@ def main(argv=None):
         return 0
     dist = Dist()
     try:
-        result = run_config4(args, dist) if args.config == 4 else run_ours(args, dist)
+        runner = {4: run_config4, 5: run_config5}.get(args.config, run_ours)
+        result = runner(args, dist)
         if dist.rank == 0:
             print(json.dumps(result), flush=True)
     finally:
