@@ -973,8 +973,18 @@ def run_reference(args, dist: Dist):
     }
 
 
+def _result_stream():
+    """Keep stdout for the one JSON line: send everything else written to fd 1
+    (NCCL's version banner, library prints) to stderr."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    return os.fdopen(saved, "w")
+
+
 def main(argv=None):
     args = parse_args(argv)
+    out = _result_stream()
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
@@ -983,14 +993,14 @@ def main(argv=None):
 
         world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
         result = run_reference(args, SimpleNamespace(rank=0, world=world))
-        print(json.dumps(result), flush=True)
+        print(json.dumps(result), file=out, flush=True)
         return 0
     dist = Dist()
     try:
         runner = {4: run_config4, 5: run_config5}.get(args.config, run_ours)
         result = runner(args, dist)
         if dist.rank == 0:
-            print(json.dumps(result), flush=True)
+            print(json.dumps(result), file=out, flush=True)
     finally:
         dist.close()
     return 0
