@@ -171,7 +171,10 @@ __device__ __forceinline__ void copy_row_any(const GatherParams& p, bool valid, 
 // byte offset in lane k's `mine`) when a row is small: the (row, plane, vector)
 // space is flattened so that the kUnroll vectors each lane keeps in flight span
 // several rows.  Every address must be 16-byte aligned.
-constexpr uint32_t kFlatRowLimit = 32 * kUnroll;  // vectors per row (all planes) below which to flatten
+#ifndef EKV_GATHER_FLAT_LIMIT
+#define EKV_GATHER_FLAT_LIMIT (32 * kUnroll)
+#endif
+constexpr uint32_t kFlatRowLimit = EKV_GATHER_FLAT_LIMIT;  // vectors per row (all planes) up to which to flatten
 
 __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t mine, int64_t row0,
                                                  int64_t warps, int nb, unsigned lane) {
