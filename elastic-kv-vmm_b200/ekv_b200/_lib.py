@@ -194,8 +194,13 @@ def i64_array(values) -> ct.Array:
     return (ct.c_int64 * max(1, len(values)))(*values)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
     """Raw cudaStream_t of torch's current stream on `device` (0 = legacy default)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -214,11 +219,12 @@ def require_cuda(tensors: dict, device: torch.device | None = None) -> torch.dev
     for name, tensor in tensors.items():
         if tensor is None:
             continue
-        if not isinstance(tensor, torch.Tensor) or tensor.device.type != "cuda":
+        if not isinstance(tensor, torch.Tensor) or not tensor.is_cuda:
             raise ValueError(f"{name} must be a CUDA tensor")
+        here = tensor.device
         if device is None:
-            device = tensor.device
-        elif tensor.device != device:
+            device = here
+        elif here != device:
             raise ValueError("all tensors must be on the same CUDA device")
     if device is None:
         raise ValueError("no CUDA tensor given")
