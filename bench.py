@@ -39,6 +39,10 @@ for _path in (str(ROOT / "elastic-kv-vmm_b200"), str(ROOT)):
     if _path not in sys.path:
         sys.path.insert(0, _path)
 
+# The fused bitmap combine reads peers through plain peer mappings; torch's symmetric
+# memory need not bind an NVSwitch multicast object for it.
+os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+
 import torch  # noqa: E402
 
 CHUNK = 2 << 20
@@ -563,6 +567,28 @@ def bitmap_bench(dist: Dist, reps: int = 50):
     end.record(stream)
     torch.cuda.synchronize()
     combine_ms = dist.max(start.elapsed_time(end) / reps)
+    fused = {}
+    if dist.world > 1:
+        # One kernel builds this rank's bitmap, publishes it in symmetric memory and ANDs
+        # the peers' words over NVLink; timed with the counts kernel in front, like
+        # build + combine above.
+        from ekv_b200.releasable import PeerFreeableCombiner
+
+        combiner = PeerFreeableCombiner(n_chunks, dev)
+        fused_joint = combiner.combine(projection.counts(candidate), refs, mapped)
+        dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(reps):
+            combiner.combine(projection.counts(candidate), refs, mapped, out=fused_joint)
+        end.record(stream)
+        torch.cuda.synchronize()
+        fused_ms = dist.max(start.elapsed_time(end) / reps)
+        fused = {"fused_build_combine_us": fused_ms * 1e3,
+                 "unfused_build_combine_us": (build_ms + combine_ms) * 1e3,
+                 "fused_matches_nccl": bool(torch.equal(fused_joint, joint)) and not combiner.failed()}
+        dist.barrier()
+        del combiner
     local_set = bitmap_to_chunks(local)
     expected_joint = set(local_set)
     for r in range(dist.world):
@@ -571,7 +597,8 @@ def bitmap_bench(dist: Dist, reps: int = 50):
             "freeable_local": len(local_set), "freeable_joint": len(bitmap_to_chunks(joint)),
             "joint_matches_intersection": bitmap_to_chunks(joint) == expected_joint,
             "build_us": build_ms * 1e3, "combine_us": combine_ms * 1e3,
-            "combine": "NCCL all_gather_into_tensor + AND kernel" if dist.world > 1 else "single rank"}
+            "combine": "NCCL all_gather_into_tensor + AND kernel" if dist.world > 1 else "single rank",
+            **fused}
 
 
 # --------------------------------------------------------------------------- arms

@@ -119,6 +119,8 @@ _KERNELS = {
     ],
     "ekv_freeable_bitmap": [_p, _p, _p, _i64, _p, _i32, _p],
     "ekv_bitmap_and": [_p, _i32, _i64, _p, _i32, _p],
+    "ekv_freeable_and_peers": [_p, _p, _p, _p, _i64, _u64p, _i32, _i32, ct.c_uint32, ct.c_uint32,
+                               _p, _p, _p, _i32, _p],
     "ekv_device_status": [_i32, ct.POINTER(ct.c_uint), _i32],
 }
 

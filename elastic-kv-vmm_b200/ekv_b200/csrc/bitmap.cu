@@ -239,3 +239,165 @@ extern "C" int ekv_bitmap_and(
         check_launch("bitmap_and launch");
     });
 }
+
+// ---------------------------------------------------------------- fused build + cross-rank AND over peer memory
+//
+// The joint-demotion decision is a compute step (this rank's freeable bitmap)
+// followed by a collective (AND over the tensor-parallel ranks).  Instead of an
+// NCCL all-gather and a second kernel, one single-block kernel per rank:
+//   1. builds its bitmap and writes it into its own peer-visible buffer (slot
+//      epoch & 1: a rank can be at most one call ahead of another, so two
+//      slots never collide);
+//   2. publishes it with a system-scope release store of `epoch` into its flag
+//      slot in every peer's buffer;
+//   3. waits -- with a poll limit -- until every peer's flag in its own buffer
+//      has reached `epoch` (acquire loads);
+//   4. ANDs the peers' words, read straight from their memory over NVLink.
+// A wait that runs out sets *status and leaves `out` unwritten; the kernel
+// never hangs.  Buffer layout per rank: 64 uint32 flags (256 B), then two
+// slots of n_words uint64.  Plain peer loads and stores only.
+
+namespace ekv {
+namespace {
+
+constexpr int kPeerMaxRanks = 64;
+constexpr int kPeerFlagBytes = kPeerMaxRanks * 4;
+constexpr int kPeerThreads = 256;
+
+struct PeerParams {
+    const int32_t* counts;
+    const int32_t* refs;
+    const uint64_t* mapped;
+    const uint64_t* local_bits;
+    uint64_t* out;
+    uint64_t* local_out;
+    uint32_t* status;
+    int64_t n_chunks, n_words;
+    int n_ranks, rank;
+    uint32_t epoch, max_polls;
+    char* buffers[kPeerMaxRanks];
+};
+
+__device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t load_relaxed_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kPeerThreads, 1)
+freeable_and_peers_kernel(const __grid_constant__ PeerParams p) {
+    __shared__ int failed;
+    const unsigned lane = lane_id();
+    const int warp = threadIdx.x >> 5;
+    const int64_t slot_offset = static_cast<int64_t>(p.epoch & 1u) * p.n_words;
+    uint64_t* mine = reinterpret_cast<uint64_t*>(p.buffers[p.rank] + kPeerFlagBytes) + slot_offset;
+    if (threadIdx.x == 0) failed = 0;
+    // 1. This rank's bitmap.
+    if (p.local_bits) {
+        for (int64_t w = threadIdx.x; w < p.n_words; w += kPeerThreads) mine[w] = p.local_bits[w];
+    } else {
+        for (int64_t w = warp; w < p.n_words; w += kPeerThreads / 32) {
+            unsigned half[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int64_t c = w * 64 + h * 32 + lane;
+                bool freeable = false;
+                if (c < p.n_chunks) {
+                    const int32_t count = p.counts[c];
+                    freeable = count > 0 && count == p.refs[c];
+                }
+                half[h] = __ballot_sync(0xffffffffu, freeable);
+            }
+            if (lane == 0) {
+                const uint64_t word = ((static_cast<uint64_t>(half[1]) << 32) | half[0]) & p.mapped[w];
+                mine[w] = word;
+                if (p.local_out) p.local_out[w] = word;
+            }
+        }
+    }
+    __syncthreads();
+    // 2. Publish (the release is cumulative over the block's writes ordered by the barrier).
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int r = 0; r < p.n_ranks; ++r) {
+            if (r != p.rank) store_release_sys(reinterpret_cast<uint32_t*>(p.buffers[r]) + p.rank, p.epoch);
+        }
+    }
+    // 3. Wait for every peer, with a poll limit.
+    if (threadIdx.x < p.n_ranks && static_cast<int>(threadIdx.x) != p.rank) {
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(p.buffers[p.rank]) + threadIdx.x;
+        bool arrived = false;
+        for (uint32_t polls = 0; polls < p.max_polls; ++polls) {
+            if (static_cast<int32_t>(load_acquire_sys(flag) - p.epoch) >= 0) {
+                arrived = true;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (!arrived) atomicExch(&failed, 1);
+    }
+    __syncthreads();
+    if (failed) {
+        if (threadIdx.x == 0 && p.status) atomicOr(p.status, 1u);
+        return;
+    }
+    // 4. AND over the ranks.
+    for (int64_t w = threadIdx.x; w < p.n_words; w += kPeerThreads) {
+        uint64_t acc = mine[w];
+        for (int r = 0; r < p.n_ranks; ++r) {
+            if (r == p.rank) continue;
+            acc &= load_relaxed_sys(reinterpret_cast<const uint64_t*>(p.buffers[r] + kPeerFlagBytes) +
+                                    slot_offset + w);
+        }
+        p.out[w] = acc;
+    }
+}
+
+}  // namespace
+}  // namespace ekv
+
+extern "C" int ekv_freeable_and_peers(
+    const int32_t* counts, const int32_t* refs, const uint64_t* mapped_bits, const uint64_t* local_bits,
+    int64_t n_chunks, const uint64_t* peer_buffers, int n_ranks, int rank, uint32_t epoch,
+    uint32_t max_polls, uint64_t* out, uint64_t* local_out, uint32_t* status, int device, void* stream) {
+    return guarded([&] {
+        require(n_chunks > 0, "n_chunks must be positive");
+        require(n_ranks >= 1 && n_ranks <= kPeerMaxRanks, "rank count outside [1, 64]");
+        require(rank >= 0 && rank < n_ranks, "rank outside [0, n_ranks)");
+        require(peer_buffers && out, "null pointer argument");
+        require(local_bits || (counts && refs && mapped_bits),
+                "need either local_bits or counts, refs and mapped_bits");
+        require(max_polls > 0, "max_polls must be positive");
+        bind_device(device);
+        PeerParams p{};
+        p.counts = counts;
+        p.refs = refs;
+        p.mapped = mapped_bits;
+        p.local_bits = local_bits;
+        p.out = out;
+        p.local_out = local_out;
+        p.status = status;
+        p.n_chunks = n_chunks;
+        p.n_words = (n_chunks + 63) / 64;
+        p.n_ranks = n_ranks;
+        p.rank = rank;
+        p.epoch = epoch;
+        p.max_polls = max_polls;
+        for (int r = 0; r < n_ranks; ++r) {
+            require(peer_buffers[r] && peer_buffers[r] % 16 == 0, "peer buffers must be 16-byte aligned");
+            p.buffers[r] = reinterpret_cast<char*>(peer_buffers[r]);
+        }
+        freeable_and_peers_kernel<<<1, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        check_launch("freeable_and_peers launch");
+    });
+}

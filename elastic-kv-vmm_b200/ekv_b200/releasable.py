@@ -21,7 +21,7 @@ from typing import Callable, Iterable
 
 import torch
 
-from ._lib import MAX_PLANES, call, i64_array, index_esize, require_cuda, stream_handle
+from ._lib import MAX_PLANES, call, i64_array, index_esize, require_cuda, stream_handle, u64_array
 
 
 def words_for(n_chunks: int) -> int:
@@ -139,6 +139,65 @@ def combine_freeable(bitmap: torch.Tensor, group=None, *,
     if and_fn is not None:
         return and_fn(gathered)
     return bitmap_and(gathered)
+
+
+PEER_FLAG_BYTES = 256  # 64 uint32 arrival flags at the head of each rank's buffer
+
+
+class PeerFreeableCombiner:
+    """Freeable bitmap + cross-rank AND in one kernel over peer (symmetric) memory.
+
+    Every rank of ``group`` builds one combiner (a collective: it allocates and
+    exchanges the peer buffers) and then calls ``combine`` in the same order.
+    ``buffers`` may instead be given directly as a list of peer-visible device
+    addresses (rank order) with ``rank``; that form serves tests.
+    ``max_polls`` bounds each wait for a peer (~64 ns per poll).
+    """
+
+    def __init__(self, n_chunks: int, device, group=None, *, buffers=None, rank=None,
+                 max_polls: int = 1 << 24):
+        self.n_chunks = int(n_chunks)
+        self.n_words = words_for(self.n_chunks)
+        self.device = torch.device(device)
+        self.max_polls = int(max_polls)
+        self.epoch = 0
+        self._keep = None
+        if buffers is None:
+            import torch.distributed as dist
+            import torch.distributed._symmetric_memory as symm_mem
+
+            nbytes = PEER_FLAG_BYTES + 2 * 8 * self.n_words
+            local = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+            local.zero_()
+            handle = symm_mem.rendezvous(local, group if group is not None else dist.group.WORLD)
+            handle.barrier()
+            buffers = list(handle.buffer_ptrs)
+            rank = handle.rank
+            self._keep = (local, handle)
+        if rank is None:
+            raise ValueError("rank is required with explicit buffers")
+        self.rank = int(rank)
+        self.n_ranks = len(buffers)
+        self._buffers = u64_array(buffers)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def combine(self, counts=None, refs=None, mapped_bits=None, *, local_bits=None, out=None, local_out=None):
+        """AND over the ranks of every rank's freeable bitmap; returns ``out`` (int64 words)."""
+        if out is None:
+            out = torch.empty(self.n_words, dtype=torch.int64, device=self.device)
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        call("ekv_freeable_and_peers",
+             None if counts is None else counts.data_ptr(), None if refs is None else refs.data_ptr(),
+             None if mapped_bits is None else mapped_bits.data_ptr(),
+             None if local_bits is None else local_bits.data_ptr(), self.n_chunks, self._buffers,
+             self.n_ranks, self.rank, self.epoch, self.max_polls, out.data_ptr(),
+             None if local_out is None else local_out.data_ptr(), self.status.data_ptr(),
+             self.device.index, stream_handle(self.device))
+        return out
+
+    def failed(self) -> bool:
+        """True once a wait for a peer ran out (synchronizes with the device)."""
+        return bool(self.status.item())
 
 
 class FreeableChunks:

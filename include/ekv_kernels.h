@@ -293,6 +293,24 @@ int ekv_bitmap_and(
     const uint64_t* gathered, int n_ranks, int64_t n_words, uint64_t* out,
     int device, void* stream);
 
+/*
+ * R6 — freeable bitmap and its AND over the tensor-parallel ranks in ONE kernel,
+ * over peer memory instead of an NCCL all-gather (same result as
+ * ekv_freeable_bitmap + all-gather + ekv_bitmap_and).  Every rank launches it with
+ * the same `epoch` (a call counter starting at 1).  peer_buffers is a HOST array
+ * of n_ranks device addresses (rank r's peer-visible buffer, e.g. symmetric
+ * memory; 256 + 16 * n_words bytes, zeroed once before the first call);
+ * peer_buffers[rank] is this rank's own.  The local bitmap is either built from
+ * counts / refs / mapped_bits or taken from local_bits.  A rank waits at most
+ * max_polls polls (~64 ns apart) for each peer; if one does not arrive, *status
+ * (device uint32, may be NULL) gets bit 0 and `out` is not written.
+ * local_out (may be NULL) receives this rank's own bitmap.
+ */
+int ekv_freeable_and_peers(
+    const int32_t* counts, const int32_t* refs, const uint64_t* mapped_bits, const uint64_t* local_bits,
+    int64_t n_chunks, const uint64_t* peer_buffers, int n_ranks, int rank, uint32_t epoch,
+    uint32_t max_polls, uint64_t* out, uint64_t* local_out, uint32_t* status, int device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,18 @@ def _worker(rank, world, port, backend, n_chunks, results):
         if backend == "nccl":
             joint = combine_freeable(local)
             torch.cuda.synchronize()
+            # The fused peer-memory combine agrees with the NCCL path, epoch after epoch.
+            from ekv_b200.releasable import PeerFreeableCombiner
+
+            combiner = PeerFreeableCombiner(n_chunks, device)
+            for epoch in range(6):
+                bits = chunks_to_bitmap(_rank_bitmap(rank + 10 * epoch, n_chunks), n_chunks, device)
+                fused = combiner.combine(local_bits=bits)
+                reference = combine_freeable(bits)
+                torch.cuda.synchronize()
+                assert torch.equal(fused, reference), f"epoch {epoch}"
+            assert not combiner.failed()
+            del combiner
         else:
             joint = combine_freeable(local, and_fn=lambda g: torch.from_numpy(bitmap_and_np(g.numpy())))
         results[rank] = sorted(bitmap_to_chunks(joint))
@@ -96,6 +108,9 @@ def test_combine_freeable_nccl(cuda_device):
     if world < 2:
         pytest.skip("needs two or more GPUs")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    # The peer combine reads plain peer mappings; keep torch's symmetric memory unbound
+    # from any NVSwitch multicast object.
+    os.environ["TORCH_SYMM_MEM_DISABLE_MULTICAST"] = "1"
     _run(min(world, 8), "nccl")
 
 

@@ -121,3 +121,75 @@ def test_freeable_chunks_tracker_view(cuda_device):
     c = case["candidates"]
     assert sorted(freeable.releasable_group([c[0], c[1]])) == case["pair"]
     assert sorted(freeable.releasable_group(c)) == case["group"]
+
+
+def _peer_inputs(gen, n_chunks, device):
+    refs = torch.randint(0, 4, (n_chunks,), generator=gen).to(torch.int32)
+    counts = torch.where(torch.rand(n_chunks, generator=gen) < 0.6, refs,
+                         torch.randint(0, 4, (n_chunks,), generator=gen).to(torch.int32))
+    mapped = torch.randint(-(1 << 62), 1 << 62, ((n_chunks + 63) // 64,), generator=gen)
+    return counts.to(device), refs.to(device), mapped.to(device)
+
+
+def test_peer_combine_single_rank_equals_freeable_bitmap(cuda_device):
+    from ekv_b200.releasable import PEER_FLAG_BYTES, PeerFreeableCombiner, freeable_bitmap
+
+    gen = torch.Generator().manual_seed(21)
+    n = 4099
+    buf = torch.zeros(PEER_FLAG_BYTES + 2 * 8 * ((n + 63) // 64), dtype=torch.uint8, device=cuda_device)
+    combiner = PeerFreeableCombiner(n, cuda_device, buffers=[buf.data_ptr()], rank=0, max_polls=1000)
+    for _ in range(3):
+        counts, refs, mapped = _peer_inputs(gen, n, cuda_device)
+        assert torch.equal(combiner.combine(counts, refs, mapped), freeable_bitmap(counts, refs, mapped))
+    assert not combiner.failed()
+
+
+def test_peer_combine_two_ranks_with_the_peer_already_arrived(cuda_device):
+    """Rank 0 of two, the peer's flag and bitmap already in place (written from the host):
+    one kernel, nothing to wait for but the flag, result = AND of both bitmaps."""
+    from ekv_b200.releasable import PEER_FLAG_BYTES, PeerFreeableCombiner, freeable_bitmap
+
+    gen = torch.Generator().manual_seed(22)
+    n = 3000
+    words = (n + 63) // 64
+    size = PEER_FLAG_BYTES + 2 * 8 * words
+    mine = torch.zeros(size, dtype=torch.uint8, device=cuda_device)
+    peer = torch.zeros(size, dtype=torch.uint8, device=cuda_device)
+    combiner = PeerFreeableCombiner(n, cuda_device, buffers=[mine.data_ptr(), peer.data_ptr()], rank=0,
+                                    max_polls=100000)
+    for epoch in (1, 2, 3):
+        peer_bits = torch.randint(-(1 << 62), 1 << 62, (words,), generator=gen).to(cuda_device)
+        slot = (epoch & 1) * words
+        peer.view(torch.int64)[PEER_FLAG_BYTES // 8 + slot: PEER_FLAG_BYTES // 8 + slot + words] = peer_bits
+        mine.view(torch.int32)[1] = epoch  # the peer (rank 1) has published this epoch
+        torch.cuda.synchronize()
+        counts, refs, mapped = _peer_inputs(gen, n, cuda_device)
+        local = torch.empty(words, dtype=torch.int64, device=cuda_device)
+        out = combiner.combine(counts, refs, mapped, local_out=local)
+        torch.cuda.synchronize()
+        assert torch.equal(local, freeable_bitmap(counts, refs, mapped))
+        assert torch.equal(out, local & peer_bits)
+        assert int(peer.view(torch.int32)[0]) == epoch  # our arrival flag landed in the peer's buffer
+    assert not combiner.failed()
+
+
+def test_peer_combine_wait_gives_up_with_a_status(cuda_device):
+    """A peer that never arrives: the bounded wait runs out, the status word is set and
+    the output is left untouched -- no hang, the context stays usable."""
+    from ekv_b200.releasable import PEER_FLAG_BYTES, PeerFreeableCombiner
+
+    n = 640
+    size = PEER_FLAG_BYTES + 2 * 8 * 10
+    mine = torch.zeros(size, dtype=torch.uint8, device=cuda_device)
+    absent = torch.zeros(size, dtype=torch.uint8, device=cuda_device)
+    combiner = PeerFreeableCombiner(n, cuda_device, buffers=[mine.data_ptr(), absent.data_ptr()], rank=0,
+                                    max_polls=2000)
+    out = torch.full((10,), 12345, dtype=torch.int64, device=cuda_device)
+    bits = torch.full((10,), -1, dtype=torch.int64, device=cuda_device)
+    combiner.combine(local_bits=bits, out=out)
+    assert combiner.failed()
+    assert (out == 12345).all()
+    # The context is still usable: the next launch (the single-rank form) completes.
+    alone = PeerFreeableCombiner(n, cuda_device, buffers=[mine.data_ptr()], rank=0, max_polls=10)
+    assert torch.equal(alone.combine(local_bits=bits), bits)
+    assert not alone.failed()
