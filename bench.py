@@ -13,10 +13,13 @@ Extra keys: ``e2e`` (public Python API per step, positions copied from pinned
 host memory and one result row read back), ``roofline`` (gather kernel vs the
 measured HBM copy peak), ``cpu_baseline`` (torch-CPU restatement on the host
 cores, bounded sample), ``migration`` (config 3: 256 victim chunks packed into
-2 MiB-aligned pinned staging and restored into fresh VMM chunks with permuted
-slots; host-link GB/s per direction), ``bitmap`` (config 4 geometry: freeable
-bitmap build and the NCCL AND-combine latency), ``clocks`` (NVML samples
-during the timed region).
+pinned host staging through the copy-engine ring and restored into fresh VMM
+chunks with permuted slots; host-link GB/s per direction), ``lookup``
+(config 1 lookups, resolve_resident at the reference's microbenchmark shape,
+shared-prefix donor resolution at the config-5 shape), ``bitmap`` (config 4
+geometry: freeable bitmap build, the NCCL AND-combine latency and, for N > 1,
+the fused peer-memory combine), ``clocks`` (NVML samples during the timed
+region).
 
 ``--impl reference`` times the reference's CPU path (torch-CPU restatement,
 all host threads) on a bounded sample of the same workload.
@@ -503,6 +506,7 @@ def lookup_bench(dist: Dist, rounds: int = 20, calls: int = 100):
 
     resolve_us = p50(resolve_call)
     resolve_graph_us = graph_us(resolve_call)
+    shared = shared_prefix_bench(dev, p50, graph_us)
     expected = torch.tensor([[((rb - 1 - r) * 8192 + blk * 512 + off + 1) * 3 + 5
                               for blk in range(16) for off in range(128)] for r in range(rb)],
                             dtype=torch.int32, device=dev)
@@ -515,8 +519,57 @@ def lookup_bench(dist: Dist, rounds: int = 20, calls: int = 100):
             "resolve_resident_batch4_device_us": resolve_graph_us,
             "resolve_resident_published_a100_triton_us": 30.08,
             "resolve_resident_correct": bool(torch.equal(result[0], expected)),
+            "shared_prefix": shared,
             "timing": "p50 of per-call CUDA-event time, 100 calls per round (reference methodology, "
                       "includes host dispatch); *_device_us: the same 100 calls replayed from one CUDA graph"}
+
+
+def shared_prefix_bench(dev, p50, graph_us):
+    """Shared-prefix donor-slot resolution at the config-5 shape: 128 consumers x
+    2048 Top-K blocks of one token, 65536-token request table, 1 Mi-slot mapping.
+    Public API per call (includes the host -> device copy of the per-request
+    lists), device time of the kernel alone (CUDA graph), and the reference's torch
+    expression on the host cores for the same inputs."""
+    from ekv_b200 import shared_prefix as sp
+    from oracle.cpu_baseline import torch_shared_resolver
+
+    requests, topk, ctx, slots = 128, 2048, 65536, 1 << 20
+    gen = torch.Generator().manual_seed(8)
+    table = torch.randint(0, slots, (requests, ctx), generator=gen, dtype=torch.int32)
+    mapping = torch.randint(0, 1 << 22, (slots,), generator=gen, dtype=torch.int64)
+    blocks = torch.randint(0, ctx, (requests, topk), generator=gen, dtype=torch.int32)
+    rows = torch.randint(0, requests, (requests,), generator=gen)
+    prefixes = torch.randint(0, ctx, (requests,), generator=gen)
+    lengths = torch.full((requests,), ctx, dtype=torch.int64)
+    d_table, d_mapping, d_blocks, d_lengths = (t.to(dev) for t in (table, mapping, blocks, lengths))
+    rows_l, prefixes_l = rows.tolist(), prefixes.tolist()
+
+    def api_call():
+        return sp.resolve_shared_block_locations_batched(
+            d_blocks, source_rows=rows_l, seq_len=d_lengths, shared_tokens=prefixes_l, block_size=1,
+            request_table=d_table, device_mapping=d_mapping)
+
+    valid, physical = api_call()
+    meta = torch.cat([rows, prefixes]).to(dev)
+
+    def kernel_call():
+        sp._launch(d_blocks, requests, topk, d_blocks.stride(0), d_blocks.stride(1), meta[:requests], 0,
+                   meta[requests:], 0, d_lengths, 1, 1, d_table, d_mapping, valid, physical, None, False)
+
+    api_us = p50(api_call)
+    device_us = graph_us(kernel_call)
+    want_valid, want_physical = torch_shared_resolver(blocks, rows, prefixes, lengths, 1, table, mapping)
+    correct = bool(torch.equal(valid.cpu(), want_valid)) and bool(torch.equal(physical.cpu(), want_physical))
+    torch.set_num_threads(os.cpu_count() or 1)
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        torch_shared_resolver(blocks, rows, prefixes, lengths, 1, table, mapping)
+    cpu_us = (time.perf_counter() - t0) / reps * 1e6
+    return {"shape": "128 x 2048 blocks, block_size 1, table 128 x 65536 int32, mapping 1Mi int64",
+            "api_us": api_us, "device_us": device_us, "blocks_per_s_device": requests * topk / (device_us * 1e-6),
+            "reference_torch_cpu_us": cpu_us, "cpu_threads": torch.get_num_threads(), "correct": correct,
+            "shared_blocks": int(want_valid.sum())}
 
 
 # --------------------------------------------------------------------------- bitmap (config 4 geometry)

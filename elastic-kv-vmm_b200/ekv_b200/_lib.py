@@ -15,6 +15,7 @@ import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "lib" / "libekv_b200.so"
 MAX_PLANES = 256  # EKV_MAX_PLANES
+SHARED_INLINE_MAX = 512  # EKV_SHARED_INLINE_MAX
 
 _p = ct.c_void_p
 _i32 = ct.c_int
@@ -121,6 +122,14 @@ _KERNELS = {
     "ekv_bitmap_and": [_p, _i32, _i64, _p, _i32, _p],
     "ekv_freeable_and_peers": [_p, _p, _p, _p, _i64, _u64p, _i32, _i32, ct.c_uint32, ct.c_uint32,
                                _p, _p, _p, _i32, _p],
+    "ekv_resolve_shared_blocks": [
+        _p, _i32, _i64, _i64, _i64, _i64,
+        _p, _i64, _p, _i64,
+        _p, _i32, _i64, _i64,
+        _p, _i32, _i64, _i64, _i64, _i64,
+        _p, _i32, _i64, _i64,
+        _i32, _p, _p, _p, _i32, _i32, _p,
+    ],
     "ekv_device_status": [_i32, ct.POINTER(ct.c_uint), _i32],
 }
 

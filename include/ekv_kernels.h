@@ -30,6 +30,8 @@ extern "C" {
 
 /* Largest number of planes (K/V tensors of individual layers) one call takes. */
 #define EKV_MAX_PLANES 256
+/* Most requests whose host-side shared-prefix metadata fits the launch parameters. */
+#define EKV_SHARED_INLINE_MAX 512
 
 /* Thread-local message of the last failed call on this thread. */
 const char* ekv_error(void);
@@ -310,6 +312,38 @@ int ekv_freeable_and_peers(
     const int32_t* counts, const int32_t* refs, const uint64_t* mapped_bits, const uint64_t* local_bits,
     int64_t n_chunks, const uint64_t* peer_buffers, int n_ranks, int rank, uint32_t epoch,
     uint32_t max_polls, uint64_t* out, uint64_t* local_out, uint32_t* status, int device, void* stream);
+
+/*
+ * Shared-prefix donor-slot resolution, batched — replaces
+ * resolve_shared_block_locations_batched (adaptive_sparse/shared_prefix.py:122-204;
+ * the scalar form :70-119 is requests = 1) called at
+ * adaptive_sparse/request_residency.py:210-218.
+ *
+ * block_ids [requests, per_request] (int32/int64, strides block_row / block_col
+ * elements).  source_rows / shared_tokens: int64 [requests] in device memory, or
+ * NULL to use the scalar source_row / shared_count for every request; with
+ * meta_on_host != 0 both are HOST arrays of at most EKV_SHARED_INLINE_MAX
+ * entries, copied into the launch parameters (no device copy; reusable as soon
+ * as the call returns).  seq_len
+ * [requests] (stride len_stride; 0 broadcasts one value).  request_table
+ * [table_rows, table_width] with strides table_row / table_col; device_mapping
+ * [map_len] with stride map_stride.  Outputs: valid uint8 [requests, per_request]
+ * and physical int32 [requests, per_request, block_size] (contiguous).
+ * masked_blocks (may be NULL, may alias block_ids, same esize and strides)
+ * receives -1 where the block is valid and the block id elsewhere, the caller's
+ * masked_fill (request_residency.py:231).  exclude_newest != 0 also requires
+ * (block + 1) * block_size < seq_len (request_residency.py:220).
+ * Source rows must lie in [0, table_rows) (the Python API checks this, as the
+ * reference does); a row outside resolves to slot 0 and an invalid block.
+ */
+int ekv_resolve_shared_blocks(
+    const void* block_ids, int block_esize, int64_t requests, int64_t per_request, int64_t block_row,
+    int64_t block_col, const int64_t* source_rows, int64_t source_row, const int64_t* shared_tokens,
+    int64_t shared_count, const void* seq_len, int len_esize, int64_t len_stride, int64_t block_size,
+    const void* request_table, int table_esize, int64_t table_rows, int64_t table_width, int64_t table_row,
+    int64_t table_col, const void* device_mapping, int map_esize, int64_t map_len, int64_t map_stride,
+    int meta_on_host, uint8_t* valid, int32_t* physical, void* masked_blocks, int exclude_newest, int device,
+    void* stream);
 
 #ifdef __cplusplus
 }

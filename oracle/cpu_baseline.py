@@ -49,3 +49,20 @@ def torch_resolver(topk, table, mapping, rows, lengths, selected, result, block_
     valid = (positions >= 0) & (positions < lengths[selected, None])
     logical = table[rows[selected, None], positions.masked_fill(~valid, 0)]
     result[0, selected] = mapping[logical].masked_fill(~valid, -1).to(torch.int32)
+
+
+def torch_shared_resolver(block_ids, rows, prefixes, seq_len, block_size, request_table, device_mapping):
+    """The reference's batched shared-prefix resolver expression
+    (adaptive_sparse/shared_prefix.py:188-204) on any device; rows / prefixes are
+    int64 tensors."""
+    blocks = block_ids.to(torch.long)
+    starts = blocks * block_size
+    ends = starts + block_size
+    valid = (blocks >= 0) & (ends <= prefixes.reshape(-1, 1)) & (ends <= seq_len.reshape(-1, 1))
+    positions = starts.unsqueeze(2) + torch.arange(block_size, device=blocks.device, dtype=torch.long)
+    safe_positions = positions.clamp(0, request_table.shape[1] - 1)
+    logical = request_table[rows.reshape(-1, 1, 1), safe_positions]
+    safe_logical = logical.clamp(0, device_mapping.numel() - 1)
+    physical = device_mapping[safe_logical]
+    valid = valid & (logical >= 0).all(dim=2) & (physical > 0).all(dim=2)
+    return valid, physical.to(torch.int32)

@@ -34,14 +34,14 @@ def _import_reference():
     sys.path.insert(0, str(REFERENCE))
     import torch  # noqa: F401
 
-    from adaptive_sparse import minimax_vmm, migration, scheduler_budget
+    from adaptive_sparse import minimax_vmm, migration, scheduler_budget, shared_prefix
     from adaptive_sparse.resident_lookup import resolve_resident
     from experimental.sparse_read import gather_rows
     from experimental.virtual_layout import VirtualKVLayout
 
     return dict(resolve_resident=resolve_resident, gather_rows=gather_rows,
                 VirtualKVLayout=VirtualKVLayout, PhysicalPages=minimax_vmm.PhysicalPages,
-                scheduler_budget=scheduler_budget, migration=migration)
+                scheduler_budget=scheduler_budget, migration=migration, shared_prefix=shared_prefix)
 
 
 def lookup_cases(ref):
@@ -238,6 +238,72 @@ def plan_demote_cases(ref):
     return cases
 
 
+def shared_prefix_cases(ref):
+    """resolve_shared_block_locations[_batched] (adaptive_sparse/shared_prefix.py:70-204).
+
+    The vectors of tests/test_shared_prefix.py:146-228 plus seeded batches over
+    block sizes 1..100, int32 / int64 tables, unmapped and negative slots,
+    out-of-range and wrapping block ids, and slots above 2^31 (int32 wrap).
+    """
+    import torch
+
+    sp = ref["shared_prefix"]
+    cases = {}
+
+    def batched(name, blocks, rows, lengths, prefixes, block_size, table, mapping):
+        valid, physical = sp.resolve_shared_block_locations_batched(
+            blocks, source_rows=rows, seq_len=lengths, shared_tokens=prefixes, block_size=block_size,
+            request_table=table, device_mapping=mapping)
+        cases[name] = dict(block_ids=blocks.numpy(), source_rows=np.asarray(rows, dtype=np.int64),
+                           seq_len=lengths.numpy(), shared_tokens=np.asarray(prefixes, dtype=np.int64),
+                           block_size=np.int64(block_size), request_table=table.numpy(),
+                           device_mapping=mapping.numpy(), valid=valid.numpy(), physical=physical.numpy())
+
+    # tests/test_shared_prefix.py:146-152 and :188-196.
+    table2 = torch.tensor([[10, 11, 12, 13, 14, 15], [20, 21, 22, 23, 24, 25]])
+    mapping30 = torch.arange(30, dtype=torch.long)
+    mapping30[21] = 0
+    for name, blocks, row in (("scalar_a", [0, 1, 2], 0), ("scalar_b", [0, 1], 1), ("scalar_c", [0, 99], 0)):
+        valid, physical = sp.resolve_shared_block_locations(
+            torch.tensor(blocks), source_row=row, seq_len=torch.tensor(6), shared_tokens=4, block_size=2,
+            request_table=table2, device_mapping=mapping30)
+        cases[name] = dict(block_ids=np.asarray(blocks, dtype=np.int64), source_row=np.int64(row),
+                           seq_len=np.int64(6), shared_tokens=np.int64(4), block_size=np.int64(2),
+                           request_table=table2.numpy(), device_mapping=mapping30.numpy(),
+                           valid=valid.numpy(), physical=physical.numpy())
+    table3 = torch.tensor([[10, 11, 12, 13, 14, 15], [20, 21, 22, 23, 24, 25], [30, 31, 32, 33, 34, 35]])
+    mapping40 = torch.arange(40, dtype=torch.long)
+    mapping40[21] = 0
+    batched("batched_test", torch.tensor([[0, 1, 2], [1, 2, 3], [0, 1, 9]]), [0, 1, 2],
+            torch.tensor([6, 4, 6]), [4, 4, 2], 2, table3, mapping40)
+
+    gen = torch.Generator().manual_seed(2024)
+    for i, block_size in enumerate((1, 2, 3, 8, 16, 32, 64, 100)):
+        requests, per_request, table_rows, width = 7, 33, 5, 40 * block_size + 7
+        slots = 4096
+        dtype = torch.int32 if i % 2 else torch.int64
+        table = torch.randint(-3, slots, (table_rows, width), generator=gen, dtype=torch.int64)
+        table[table < 0] = -1
+        table = table.to(dtype)
+        mapping = torch.randint(1, 1 << 20, (slots,), generator=gen, dtype=torch.int64)
+        # Unmapped (0) and negative slots, rarer for wide blocks so some of those stay valid.
+        mapping[torch.rand(slots, generator=gen) < 0.1 / block_size] = 0
+        mapping[torch.rand(slots, generator=gen) < 0.05 / block_size] = -5
+        mapping[:8] = (1 << 32) + 77  # slots above 2^31: the int32 result wraps
+        blocks = torch.randint(-2, 48, (requests, per_request), generator=gen, dtype=torch.int64)
+        rows = torch.randint(0, table_rows, (requests,), generator=gen).tolist()
+        lengths = torch.randint(1, width + 64, (requests,), generator=gen, dtype=torch.int64)
+        prefixes = torch.randint(0, width + 64, (requests,), generator=gen).tolist()
+        prefixes[0] = width + 1000
+        batched(f"random_bs{block_size}", blocks.to(torch.int32 if i % 3 == 0 else torch.int64), rows,
+                lengths, prefixes, block_size, table, mapping)
+    # Block ids whose start wraps int64 (2^62 * 4 = 2^64 -> 0), as torch's int64 arithmetic does.
+    huge = torch.tensor([[1 << 62, (1 << 62) + 1, -(1 << 62), 3]], dtype=torch.int64)
+    batched("wrapping_blocks", huge, [0], torch.tensor([100]), [100], 4,
+            torch.arange(64, dtype=torch.int64).reshape(2, 32) + 1, torch.arange(200, dtype=torch.int64))
+    return cases
+
+
 def main():
     ref = _import_reference()
     np.savez_compressed(HERE / "lookup_golden.npz",
@@ -245,6 +311,9 @@ def main():
                            for key, value in arrays.items()})
     np.savez_compressed(HERE / "gather_golden.npz",
                         **{f"{case}__{key}": value for case, arrays in gather_cases(ref).items()
+                           for key, value in arrays.items()})
+    np.savez_compressed(HERE / "shared_prefix_golden.npz",
+                        **{f"{case}__{key}": value for case, arrays in shared_prefix_cases(ref).items()
                            for key, value in arrays.items()})
     (HERE / "host_golden.json").write_text(json.dumps(
         dict(layouts=layout_cases(ref), releasable=releasable_cases(ref),

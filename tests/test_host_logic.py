@@ -419,3 +419,64 @@ def test_ctypes_arrays():
     assert list(u64_array([1, 2])) == [1, 2]
     assert isinstance(i64_array([]), ct.Array)
     assert os.path.basename(str(__file__)).startswith("test_")
+
+
+# ---------------------------------------------------------------- shared prefix (host checks)
+
+def test_complete_shared_blocks_matches_reference_answers():
+    from ekv_b200.shared_prefix import complete_shared_blocks
+
+    # tests/test_shared_prefix.py:138-144 of the reference.
+    assert complete_shared_blocks([0, 1, 2, -1], seq_len=300, shared_tokens=256, block_size=128) == (
+        True, True, False, False)
+    for kwargs in (dict(seq_len=0, shared_tokens=1, block_size=1), dict(seq_len=1, shared_tokens=-1, block_size=1),
+                   dict(seq_len=1, shared_tokens=1, block_size=True)):
+        with pytest.raises(ValueError, match="outside the supported range"):
+            complete_shared_blocks([0], **kwargs)
+    with pytest.raises(ValueError, match="block ids must be integers"):
+        complete_shared_blocks([True], seq_len=4, shared_tokens=4, block_size=1)
+
+
+def test_shared_resolvers_reject_like_the_reference():
+    """Validation runs before any device work, with the reference's messages
+    (shared_prefix.py:86-106, :137-178)."""
+    from ekv_b200.shared_prefix import resolve_shared_block_locations, resolve_shared_block_locations_batched
+
+    table = torch.arange(12).reshape(2, 6)
+    mapping = torch.arange(12)
+    scalar = dict(seq_len=torch.tensor(6), shared_tokens=4, block_size=2, request_table=table,
+                  device_mapping=mapping)
+    with pytest.raises(ValueError, match="one-dimensional"):
+        resolve_shared_block_locations(torch.zeros(2, 2, dtype=torch.long), source_row=0, **scalar)
+    with pytest.raises(ValueError, match="source row is outside"):
+        resolve_shared_block_locations(torch.tensor([0]), source_row=2, **scalar)
+    with pytest.raises(ValueError, match="geometry is empty"):
+        resolve_shared_block_locations(torch.tensor([0]), source_row=0,
+                                       **{**scalar, "device_mapping": torch.empty(0, dtype=torch.long)})
+    with pytest.raises(ValueError, match="invalid shared block geometry"):
+        resolve_shared_block_locations(torch.tensor([0]), source_row=0, **{**scalar, "shared_tokens": -1})
+    batched = dict(seq_len=torch.tensor([6]), block_size=2, request_table=table, device_mapping=mapping)
+    # tests/test_shared_prefix.py:230-242 of the reference.
+    with pytest.raises(ValueError, match="dimensions differ"):
+        resolve_shared_block_locations_batched(torch.tensor([[0, 1]]), source_rows=[0], shared_tokens=[2, 4],
+                                               **batched)
+    with pytest.raises(ValueError, match="sequence length dimensions differ"):
+        resolve_shared_block_locations_batched(torch.tensor([[0, 1]]), source_rows=[0], shared_tokens=[2],
+                                               **{**batched, "seq_len": torch.tensor([6, 6])})
+    with pytest.raises(ValueError, match="two-dimensional"):
+        resolve_shared_block_locations_batched(torch.tensor([0, 1]), source_rows=[0], shared_tokens=[2], **batched)
+    with pytest.raises(ValueError, match="must be integers"):
+        resolve_shared_block_locations_batched(torch.ones(1, 2, dtype=torch.bool), source_rows=[0],
+                                               shared_tokens=[2], **batched)
+    with pytest.raises(ValueError, match="source row is outside"):
+        resolve_shared_block_locations_batched(torch.tensor([[0]]), source_rows=[5], shared_tokens=[2], **batched)
+    with pytest.raises(ValueError, match="invalid shared prefix geometry"):
+        resolve_shared_block_locations_batched(torch.tensor([[0]]), source_rows=[0], shared_tokens=[-2], **batched)
+    # Empty batches return empty results without touching a device (shared_prefix.py:167-181).
+    valid, physical = resolve_shared_block_locations_batched(
+        torch.empty(0, 3, dtype=torch.long), source_rows=[], shared_tokens=[],
+        **{**batched, "seq_len": torch.empty(0, dtype=torch.long)})
+    assert valid.shape == (0, 3) and physical.shape == (0, 3, 2) and physical.dtype == torch.int32
+    # A CPU tensor reaching the kernel path is refused: there is no CPU fallback.
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        resolve_shared_block_locations_batched(torch.tensor([[0]]), source_rows=[0], shared_tokens=[2], **batched)

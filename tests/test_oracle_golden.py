@@ -194,3 +194,55 @@ def test_migration_oracle_round_trip():
     om.pack_rows(planes, slots, staging2, plane_index=plane_index)
     for t in range(20):
         np.testing.assert_array_equal(staging2[t], planes[plane_index[t]][slots[t]])
+
+
+# --------------------------------------------------------------------------- shared prefix
+
+from oracle import shared_prefix as osp  # noqa: E402
+
+SHARED_CASES = load_npz_cases("shared_prefix_golden.npz")
+
+
+@pytest.mark.parametrize("case", sorted(SHARED_CASES))
+def test_shared_prefix_oracle_matches_reference(case):
+    c = SHARED_CASES[case]
+    if "source_row" in c:
+        valid, physical = osp.resolve_scalar(c["block_ids"], int(c["source_row"]), int(c["seq_len"]),
+                                             int(c["shared_tokens"]), int(c["block_size"]),
+                                             c["request_table"], c["device_mapping"])
+    else:
+        valid, physical = osp.resolve_batched(c["block_ids"], c["source_rows"], c["seq_len"],
+                                              c["shared_tokens"], int(c["block_size"]), c["request_table"],
+                                              c["device_mapping"])
+    np.testing.assert_array_equal(valid, c["valid"])
+    np.testing.assert_array_equal(physical, c["physical"])
+
+
+def test_shared_prefix_known_answers():
+    """tests/test_shared_prefix.py:138-186 of the reference, as literal answers."""
+    assert osp.complete_shared_blocks([0, 1, 2, -1], 300, 256, 128) == (True, True, False, False)
+    a = SHARED_CASES["scalar_a"]
+    assert a["valid"].tolist() == [True, True, False]
+    assert a["physical"][a["valid"]].tolist() == [[10, 11], [12, 13]]
+    assert SHARED_CASES["scalar_b"]["valid"].tolist() == [False, True]
+    assert SHARED_CASES["scalar_c"]["valid"].tolist() == [True, False]
+    # The batched case equals the stacked scalar resolutions (test_shared_prefix.py:188-228).
+    b = SHARED_CASES["batched_test"]
+    for r in range(3):
+        valid, physical = osp.resolve_scalar(b["block_ids"][r], int(b["source_rows"][r]), int(b["seq_len"][r]),
+                                             int(b["shared_tokens"][r]), 2, b["request_table"],
+                                             b["device_mapping"])
+        np.testing.assert_array_equal(valid, b["valid"][r])
+        np.testing.assert_array_equal(physical, b["physical"][r])
+
+
+def test_shared_prefix_fixture_covers_the_edges():
+    """The seeded cases reach every branch: partial blocks, unmapped slots, int32 wrap."""
+    wrapped = SHARED_CASES["wrapping_blocks"]
+    # (2^62 + k) * 4 wraps to 4k: blocks 2^62 and 2^62 + 1 read positions 0-3 and 4-7.
+    assert wrapped["valid"].tolist() == [[True, True, False, True]]
+    assert wrapped["physical"][0, 1].tolist() == [5, 6, 7, 8]
+    total_valid = sum(int(SHARED_CASES[c]["valid"].sum()) for c in SHARED_CASES if c.startswith("random"))
+    total_invalid = sum(int((~SHARED_CASES[c]["valid"]).sum()) for c in SHARED_CASES if c.startswith("random"))
+    assert total_valid > 100 and total_invalid > 100
+    assert any((SHARED_CASES[c]["physical"] == 77).any() for c in SHARED_CASES if c.startswith("random"))
