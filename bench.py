@@ -16,7 +16,9 @@ cores, bounded sample), ``migration`` (config 3: 256 victim chunks packed into
 pinned host staging through the copy-engine ring and restored into fresh VMM
 chunks with permuted slots; host-link GB/s per direction), ``lookup``
 (config 1 lookups, resolve_resident at the reference's microbenchmark shape,
-shared-prefix donor resolution at the config-5 shape), ``bitmap`` (config 4
+shared-prefix donor resolution at the config-5 shape), ``shadow`` (logical-shadow
+bitwise check of one decode step at the config-2 batch, vs the reference's torch body
+on the same GPU), ``bitmap`` (config 4
 geometry: freeable bitmap build, the NCCL AND-combine latency and, for N > 1,
 the fused peer-memory combine), ``clocks`` (NVML samples during the timed
 region).
@@ -572,6 +574,76 @@ def shared_prefix_bench(dev, p50, graph_us):
             "shared_blocks": int(want_valid.sum())}
 
 
+def shadow_bench(dist: Dist, reps: int = 10):
+    """Logical-shadow check of one decode step at the config-2 batch: 64 requests x
+    2048 Top-K tokens, 2 KiB K and V rows, a 262144-slot shadow and cache (1 GiB
+    each), every token checked.  Algorithmic bytes per checked token: K and V row
+    of the cache and of the shadow (4 x 2048 B) + 17 B of indices, flags and
+    output.  The reference's torch body of the same check runs on the same GPU
+    beside it."""
+    from ekv_b200.logical_shadow import LogicalShadow
+    from oracle.cpu_baseline import torch_shadow_check
+
+    dev = dist.device
+    batch, topk, ctx, heads, dim, capacity = 64, 2048, 16384, 8 // dist.world or 1, 128, 262144
+    gen = torch.Generator(device=dev).manual_seed(5)
+    shadow = LogicalShadow(capacity, dev)
+    key = torch.randn((capacity, heads, dim), device=dev, generator=gen).to(torch.bfloat16)
+    value = torch.randn((capacity, heads, dim), device=dev, generator=gen).to(torch.bfloat16)
+    shadow.write(0, torch.arange(capacity, device=dev), key, value, (None, None))
+    phys_of = torch.randperm(capacity, device=dev, generator=gen)
+    k_cache, v_cache = torch.empty_like(key), torch.empty_like(value)
+    k_cache[phys_of], v_cache[phys_of] = key, value
+    del key, value
+    table = torch.randint(1, capacity, (batch, ctx), device=dev, generator=gen, dtype=torch.int32)
+    lengths = torch.full((batch,), ctx, device=dev, dtype=torch.int64)
+    rows = torch.arange(batch, device=dev)
+    blocks = torch.argsort(torch.rand((batch, ctx), device=dev, generator=gen), dim=1)[:, :topk]
+    blocks = blocks.to(torch.int32)[None].contiguous()
+    physical = phys_of[table[rows[:, None], blocks[0].long()].long()].to(torch.int32)[None].contiguous()
+    args = (k_cache, v_cache, table, lengths, rows, 1, blocks, physical, None, 1)
+
+    def ours():
+        return shadow.check(0, *args)
+
+    k_shadow, v_shadow, initialized = shadow.layers[0]
+
+    def reference():
+        return torch_shadow_check(k_shadow, v_shadow, initialized, *args)
+
+    def per_call_ms(fn):
+        for _ in range(2):
+            fn()
+        stream = torch.cuda.current_stream()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(reps):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / reps
+
+    shadow.counts.zero_()
+    ours_ms = per_call_ms(ours)
+    counts = shadow.counts.tolist()
+    ref_ms = per_call_ms(reference)
+    ref_counts, ref_clean, ref_phys = reference()
+    clean, phys_out = ours()
+    agree = bool(torch.equal(ref_clean, clean)) and bool(torch.equal(ref_phys, phys_out))
+    calls = counts[5]
+    row_bytes = heads * dim * 2
+    per_token = 4 * row_bytes + 17
+    achieved = batch * topk * per_token / (ours_ms * 1e-3) / 1e9
+    peak, source = measured_hbm_peak()
+    return {"shape": f"{batch} x {topk} tokens, {row_bytes} B rows, {capacity}-slot shadow and cache",
+            "check_ms": ours_ms, "tokens_per_s": batch * topk / (ours_ms * 1e-3),
+            "achieved_gbs": achieved, "peak_gbs": peak, "frac": achieved / peak, "peak_source": source,
+            "reference_torch_same_gpu_ms": ref_ms, "speedup_vs_reference_torch": ref_ms / ours_ms,
+            "checked_per_call": counts[0] / calls if calls else 0, "mismatched": counts[4],
+            "agrees_with_reference_torch": agree and ref_counts.tolist()[0] == counts[0] / calls}
+
+
 # --------------------------------------------------------------------------- bitmap (config 4 geometry)
 
 def bitmap_bench(dist: Dist, reps: int = 50):
@@ -719,6 +791,7 @@ def run_ours(args, dist: Dist):
 
     result["bitmap"] = bitmap_bench(dist)
     result["lookup"] = lookup_bench(dist)
+    result["shadow"] = shadow_bench(dist)
 
     if dist.rank == 0 and dist.world == 1 and not args.skip_cpu:
         result["cpu_baseline"] = cpu_baseline(work, args.cpu_seconds)

@@ -16,6 +16,7 @@ import torch
 LIBRARY_PATH = Path(__file__).resolve().parent / "lib" / "libekv_b200.so"
 MAX_PLANES = 256  # EKV_MAX_PLANES
 SHARED_INLINE_MAX = 512  # EKV_SHARED_INLINE_MAX
+SHADOW_MAX_LAYERS = 128  # EKV_SHADOW_MAX_LAYERS
 
 _p = ct.c_void_p
 _i32 = ct.c_int
@@ -130,6 +131,32 @@ _KERNELS = {
         _p, _i32, _i64, _i64,
         _i32, _p, _p, _p, _i32, _i32, _p,
     ],
+    "ekv_shadow_check": [
+        _p, _i32, _i64, _i64, _i64, _i64,
+        _p, _i32, _i64, _p, _i32, _i64,
+        _p, _i32, _i64, _i64, _i64,
+        _p, _i64, _i64, _p, _i64,
+        _p, _p, _i64, _i64, _i64,
+        _p, _p, _p, _i64,
+        _i64, _i64, _i64, _i64,
+        _i64, _i64, _p, _p, _p,
+        _i32, _p,
+    ],
+    "ekv_shadow_check_complete": [
+        _p, _i32, _p, _i32, _i64,
+        _i64, _i64, _i64, _p, _i64,
+        _u64p, _u64p, _u64p, _u64p,
+        _u64p, _i32, _i64, _i64,
+        _i64, _i64, _i64, _i64, _p,
+        _i32, _p,
+    ],
+    "ekv_shadow_write": [
+        _p, _p, _p, _i64, _i64,
+        _i64, _p, _p, _i64, _i64,
+        _i64, _i64, _p, _i32, _i64, _i32,
+        _p,
+    ],
+    "ekv_shadow_reset": [_u64p, _i32, _i64, _p, _i32, _i64, _i32, _p],
     "ekv_device_status": [_i32, ct.POINTER(ct.c_uint), _i32],
 }
 

@@ -25,7 +25,7 @@ INCLUDE = REPO / "include"
 BUILD_DIR = PACKAGE / "_build"
 LIBRARY = PACKAGE / "lib" / "libekv_b200.so"
 
-SOURCES = ("common.cu", "lookup.cu", "gather.cu", "migrate.cu", "swap.cu", "bitmap.cu", "shared_prefix.cu", "vmm.cpp")
+SOURCES = ("common.cu", "lookup.cu", "gather.cu", "migrate.cu", "swap.cu", "bitmap.cu", "shared_prefix.cu", "shadow.cu", "vmm.cpp")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 FLAGS = ("-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "-Werror=all-warnings")
 

@@ -32,6 +32,8 @@ extern "C" {
 #define EKV_MAX_PLANES 256
 /* Most requests whose host-side shared-prefix metadata fits the launch parameters. */
 #define EKV_SHARED_INLINE_MAX 512
+/* Most layers one logical-shadow migration check or reset covers in a launch. */
+#define EKV_SHADOW_MAX_LAYERS 128
 
 /* Thread-local message of the last failed call on this thread. */
 const char* ekv_error(void);
@@ -344,6 +346,73 @@ int ekv_resolve_shared_blocks(
     int64_t table_col, const void* device_mapping, int map_esize, int64_t map_len, int64_t map_stride,
     int meta_on_host, uint8_t* valid, int32_t* physical, void* masked_blocks, int exclude_newest, int device,
     void* stream);
+
+/*
+ * Logical-shadow checker (diagnostic bitwise validation of KV rows) — replaces
+ * the torch bodies of LogicalShadow (adaptive_sparse/logical_shadow.py:14-140).
+ * Rows are bf16 (any even byte length); every stride below is in BYTES between
+ * consecutive slots of a [slots, ...] buffer whose rows are contiguous.
+ *
+ * ekv_shadow_check — LogicalShadow.check (:45-86) for one decode step of one
+ * layer.  blocks [1, batch, n_blocks] (strides blocks_row / blocks_col
+ * elements of dims 1 and 2), lengths / rows [batch], request_table
+ * [.., table_width]; physical [1, batch, n_blocks * block_size] int32 (strides
+ * phys_row / phys_col of dims 1 and 2) or NULL (physical = logical);
+ * live_pages [live_len] uint8 or NULL (every in-range slot backed).  Caches
+ * hold cache_rows slots; the shadow holds capacity slots with an initialized
+ * flag each.  Writes clean_blocks [1, batch, n_blocks] (contiguous, blocks'
+ * element size) and physical_out [1, batch, n_blocks * block_size] int32, and
+ * ADDS to counts[7] (uint64 on the device): checked tokens, checked bytes,
+ * uninitialized logical tokens, invalid physical tokens, mismatched tokens,
+ * calls (+1), malformed Top-K blocks.  batch <= 65535.
+ */
+int ekv_shadow_check(
+    const void* blocks, int blocks_esize, int64_t batch, int64_t n_blocks, int64_t blocks_row, int64_t blocks_col,
+    const void* lengths, int len_esize, int64_t len_stride, const void* rows, int rows_esize, int64_t rows_stride,
+    const void* request_table, int table_esize, int64_t table_width, int64_t table_row, int64_t table_col,
+    const int32_t* physical, int64_t phys_row, int64_t phys_col, const uint8_t* live_pages, int64_t live_len,
+    const void* k_cache, const void* v_cache, int64_t cache_rows, int64_t k_cache_stride, int64_t v_cache_stride,
+    const void* k_shadow, const void* v_shadow, const uint8_t* initialized, int64_t capacity,
+    int64_t k_shadow_stride, int64_t v_shadow_stride, int64_t k_row_bytes, int64_t v_row_bytes,
+    int64_t block_size, int64_t page_size, void* clean_blocks, int32_t* physical_out, uint64_t* counts,
+    int device, void* stream);
+
+/*
+ * ekv_shadow_check_complete — LogicalShadow.check_complete (:88-123): for every
+ * layer and every (logical[i], physical[i]) pair, compare the pool's K/V rows
+ * at physical[i] with the shadow's at logical[i].  pool_k / pool_v / shadow_k /
+ * shadow_v / initialized are HOST arrays of n_layers device addresses (at most
+ * EKV_SHADOW_MAX_LAYERS); pool buffers hold pool_size + page_size slots.
+ * live_pages [live_len] uint8.  ADDS to counts[4]: checked tokens, checked
+ * bytes, invalid tokens, mismatched tokens (summed over the layers).
+ */
+int ekv_shadow_check_complete(
+    const void* logical, int logical_esize, const void* physical, int physical_esize, int64_t n,
+    int64_t page_size, int64_t pool_size, int64_t capacity, const uint8_t* live_pages, int64_t live_len,
+    const uint64_t* pool_k, const uint64_t* pool_v, const uint64_t* shadow_k, const uint64_t* shadow_v,
+    const uint64_t* initialized, int n_layers, int64_t pool_k_stride, int64_t pool_v_stride,
+    int64_t shadow_k_stride, int64_t shadow_v_stride, int64_t k_row_bytes, int64_t v_row_bytes, uint64_t* counts,
+    int device, void* stream);
+
+/*
+ * ekv_shadow_write — LogicalShadow.write (:30-43): shadow rows at
+ * locations[r] = key / value row r, initialized[locations[r]] = 1.  Negative
+ * locations count from the end; locations outside [-capacity, capacity) are
+ * skipped.
+ */
+int ekv_shadow_write(
+    void* k_shadow, void* v_shadow, uint8_t* initialized, int64_t capacity, int64_t k_shadow_stride,
+    int64_t v_shadow_stride, const void* key, const void* value, int64_t key_stride, int64_t value_stride,
+    int64_t k_row_bytes, int64_t v_row_bytes, const void* locations, int loc_esize, int64_t n, int device,
+    void* stream);
+
+/*
+ * ekv_shadow_reset — LogicalShadow.reset (:26-28): initialized[l][locations[r]] = 0
+ * for each of n_layers flag arrays (a HOST array of device addresses).
+ */
+int ekv_shadow_reset(
+    const uint64_t* initialized, int n_layers, int64_t capacity, const void* locations, int loc_esize, int64_t n,
+    int device, void* stream);
 
 #ifdef __cplusplus
 }

@@ -66,3 +66,39 @@ def torch_shared_resolver(block_ids, rows, prefixes, seq_len, block_size, reques
     physical = device_mapping[safe_logical]
     valid = valid & (logical >= 0).all(dim=2) & (physical > 0).all(dim=2)
     return valid, physical.to(torch.int32)
+
+
+def torch_shadow_check(k, v, initialized, k_cache, v_cache, table, lengths, rows, block_size, blocks, physical,
+                       live_pages, page_size):
+    """The reference's LogicalShadow.check body (adaptive_sparse/logical_shadow.py:50-86) as
+    plain torch ops on any device; returns (counts [7], clean_blocks, physical_out)."""
+    capacity = k.shape[0]
+    block_limit = (lengths[:, None] + block_size - 1) // block_size
+    valid_blocks = (blocks >= 0) & (blocks < block_limit)
+    prefix = valid_blocks.to(torch.int32).cumprod(-1).bool()
+    malformed = ((blocks != -1) & ~valid_blocks) | (valid_blocks & ~prefix)
+    clean_blocks = blocks.masked_fill(~prefix, -1)
+    ids = clean_blocks[0].long()
+    positions = (ids[..., None] * block_size + torch.arange(block_size, device=ids.device)).flatten(1)
+    selected = (positions >= 0) & (positions < lengths[:, None])
+    bounded = selected & (positions < table.shape[1])
+    logical = table[rows[:, None], positions.masked_fill(~bounded, 0)].long()
+    logical_valid = bounded & (logical >= page_size) & (logical < capacity)
+    logical = logical.masked_fill(~logical_valid, 0)
+    source_valid = logical_valid & initialized[logical]
+    physical = logical if physical is None else physical[0].long()
+    in_range = (physical >= page_size) & (physical < k_cache.shape[0])
+    safe = physical.masked_fill(~in_range, 0)
+    backed = in_range if live_pages is None else in_range & live_pages[safe // page_size]
+    safe = safe.masked_fill(~backed, 0)
+    same_k = (k_cache[safe].reshape(*safe.shape, -1).view(torch.int16)
+              == k[logical].reshape(*safe.shape, -1).view(torch.int16)).all(-1)
+    same_v = (v_cache[safe].reshape(*safe.shape, -1).view(torch.int16)
+              == v[logical].reshape(*safe.shape, -1).view(torch.int16)).all(-1)
+    checked = selected & source_valid & backed
+    tokens = checked.sum()
+    bytes_per_token = (k[0].numel() + v[0].numel()) * 2
+    counts = torch.stack((tokens, tokens * bytes_per_token, (selected & ~source_valid).sum(),
+                          (selected & ~backed).sum(), (checked & ~(same_k & same_v)).sum(),
+                          tokens.new_ones(()), malformed.sum()))
+    return counts, clean_blocks, physical.masked_fill(selected & ~backed, 0).to(torch.int32).unsqueeze(0)

@@ -21,6 +21,7 @@ import os
 import random
 import sys
 from pathlib import Path
+from types import SimpleNamespace
 
 import numpy as np
 
@@ -34,14 +35,15 @@ def _import_reference():
     sys.path.insert(0, str(REFERENCE))
     import torch  # noqa: F401
 
-    from adaptive_sparse import minimax_vmm, migration, scheduler_budget, shared_prefix
+    from adaptive_sparse import logical_shadow, minimax_vmm, migration, scheduler_budget, shared_prefix
     from adaptive_sparse.resident_lookup import resolve_resident
     from experimental.sparse_read import gather_rows
     from experimental.virtual_layout import VirtualKVLayout
 
     return dict(resolve_resident=resolve_resident, gather_rows=gather_rows,
                 VirtualKVLayout=VirtualKVLayout, PhysicalPages=minimax_vmm.PhysicalPages,
-                scheduler_budget=scheduler_budget, migration=migration, shared_prefix=shared_prefix)
+                scheduler_budget=scheduler_budget, migration=migration, shared_prefix=shared_prefix,
+                logical_shadow=logical_shadow)
 
 
 def lookup_cases(ref):
@@ -304,6 +306,142 @@ def shared_prefix_cases(ref):
     return cases
 
 
+def _i16(tensor):
+    return tensor.contiguous().view(torch_module().int16).numpy()
+
+
+def torch_module():
+    import torch
+
+    return torch
+
+
+def shadow_cases(ref):
+    """LogicalShadow.check / check_complete (adaptive_sparse/logical_shadow.py:45-123).
+
+    The reference class runs on CPU tensors: producer writes recorded with
+    ``write``, a cache holding those rows with a few corrupted ones, Top-K block
+    ids with clean prefixes, padding, malformed ids and blocks past the length,
+    request-table entries below the page size and above the capacity, physical
+    slots out of range or on dead pages.  Rows of 32 B, 24 B (not a multiple of
+    16) and 2 KiB.
+    """
+    import torch
+
+    LogicalShadow = ref["logical_shadow"].LogicalShadow
+    cases = {}
+    gen = torch.Generator().manual_seed(77)
+    configs = [  # (name, heads, dim, block_size, page_size, use_physical, use_live)
+        ("bs1_phys_live", 2, 8, 1, 4, True, True),
+        ("bs4_logical", 1, 12, 4, 2, False, False),
+        ("bs2_phys", 4, 64, 2, 8, True, False),
+        ("bs1_logical_live", 1, 12, 1, 4, False, True),
+    ]
+    for name, heads, dim, block_size, page_size, use_physical, use_live in configs:
+        capacity, slots, batch, k_blocks, table_rows, width = 160, 200, 5, 12, 6, 64
+        shadow = LogicalShadow(capacity, "cpu")
+        written = torch.randperm(capacity, generator=gen)[:120]
+        key = torch.randn((120, heads, dim), generator=gen).to(torch.bfloat16)
+        value = torch.randn((120, heads, dim), generator=gen).to(torch.bfloat16)
+        shadow.write(3, written, key, value, (None, 1.0))
+        k_shadow, v_shadow, initialized = shadow.layers[3]
+        # The cache mirrors the shadow through a permutation; a few rows are corrupted.
+        # With explicit physical slots the cache holds logical slot l at phys_of[l];
+        # without, physical == logical.
+        perm = torch.randperm(slots, generator=gen)
+        k_cache = torch.randn((slots, heads, dim), generator=gen).to(torch.bfloat16)
+        v_cache = torch.randn((slots, heads, dim), generator=gen).to(torch.bfloat16)
+        phys_of = perm[:capacity] if use_physical else torch.arange(capacity)
+        k_cache[phys_of] = k_shadow
+        v_cache[phys_of] = v_shadow
+        for bad in torch.randperm(capacity, generator=gen)[:12].tolist():
+            target = k_cache if bad % 2 else v_cache
+            target[phys_of[bad], 0, bad % dim] = torch.tensor(123.5, dtype=torch.bfloat16)
+        table = torch.randint(0, capacity + 20, (table_rows, width), generator=gen, dtype=torch.int32)
+        lengths = torch.randint(1, width + 4, (batch,), generator=gen, dtype=torch.int64)
+        rows = torch.randint(0, table_rows, (batch,), generator=gen, dtype=torch.int64)
+        limit = (lengths + block_size - 1) // block_size
+        blocks = torch.full((1, batch, k_blocks), -1, dtype=torch.int32)
+        for b in range(batch):
+            n_valid = int(torch.randint(0, k_blocks + 1, (1,), generator=gen))
+            ids = torch.randint(0, int(limit[b]), (n_valid,), generator=gen)
+            blocks[0, b, :n_valid] = ids.to(torch.int32)
+            if b == 1 and n_valid < k_blocks - 2:   # valid id after padding: malformed
+                blocks[0, b, n_valid + 1] = 0
+            if b == 2:                              # id past the length: malformed, ends the prefix
+                blocks[0, b, min(n_valid, k_blocks - 1)] = int(limit[b]) + 3
+        physical = None
+        if use_physical:
+            positions = (blocks[0].long().clamp(min=0)[..., None] * block_size
+                         + torch.arange(block_size)).flatten(1).clamp(max=width - 1)
+            logical_guess = table[rows[:, None], positions]
+            physical = phys_of[logical_guess.clamp(max=capacity - 1).long()].to(torch.int32)[None]
+            physical[0, 0, :3] = torch.tensor([slots + 5, 1, -4], dtype=torch.int32)  # out of range
+        live = None
+        if use_live:
+            live = torch.rand(slots // page_size + 1, generator=gen) < 0.85
+        clean, phys_out = shadow.check(3, k_cache, v_cache, table, lengths, rows, block_size, blocks,
+                                       physical, live, page_size)
+        case = dict(k_shadow=_i16(k_shadow), v_shadow=_i16(v_shadow), initialized=initialized.numpy(),
+                    k_cache=_i16(k_cache), v_cache=_i16(v_cache), table=table.numpy(), lengths=lengths.numpy(),
+                    rows=rows.numpy(), block_size=np.int64(block_size), blocks=blocks.numpy(),
+                    page_size=np.int64(page_size), counts=shadow.counts.numpy().copy(),
+                    clean_blocks=clean.numpy(), physical_out=phys_out.numpy())
+        if physical is not None:
+            case["physical"] = physical.numpy()
+        if live is not None:
+            case["live_pages"] = live.numpy()
+        cases["check_" + name] = case
+
+    # check_complete over a 3-layer pool.
+    for name, heads, dim, page_size in (("complete_small", 2, 8, 4), ("complete_odd", 1, 12, 2)):
+        capacity, size, n_layers = 96, 128, 3
+        shadow = LogicalShadow(capacity, "cpu")
+        pool_k, pool_v = [], []
+        logical = torch.randperm(capacity - page_size, generator=gen)[:60] + page_size
+        physical = torch.randperm(size, generator=gen)[:60] + page_size
+        for layer in range(n_layers):
+            written = torch.randperm(capacity, generator=gen)[:80]
+            key = torch.randn((80, heads, dim), generator=gen).to(torch.bfloat16)
+            value = torch.randn((80, heads, dim), generator=gen).to(torch.bfloat16)
+            shadow.write(10 + layer, written, key, value, (None, None))
+            k, v, _ = shadow.layers[10 + layer]
+            pk = torch.randn((size + page_size, heads, dim), generator=gen).to(torch.bfloat16)
+            pv = torch.randn((size + page_size, heads, dim), generator=gen).to(torch.bfloat16)
+            pk[physical] = k[logical]
+            pv[physical] = v[logical]
+            for bad in range(layer, 60, 17):
+                (pk if bad % 2 else pv)[physical[bad], 0, 0] = torch.tensor(-7.25, dtype=torch.bfloat16)
+            pool_k.append(pk)
+            pool_v.append(pv)
+        logical[5] = 1            # below the page size
+        logical[6] = capacity + 3  # past the capacity
+        physical[7] = size + page_size + 1  # past the pool
+        pages = sorted(set(range(1, size // page_size + 1)) - {int(physical[9]) // page_size})
+        pool = SimpleNamespace(page_size=page_size, size=size, adaptive_vmm=SimpleNamespace(pages=set(pages)),
+                               start_layer=10, end_layer=10 + n_layers,
+                               get_key_buffer=lambda layer, pk=pool_k: pk[layer - 10],
+                               get_value_buffer=lambda layer, pv=pool_v: pv[layer - 10])
+        try:
+            shadow.check_complete(pool, logical, physical, "test")
+            raised = False
+        except RuntimeError:
+            raised = True
+        case = dict(logical=logical.numpy(), physical=physical.numpy(), page_size=np.int64(page_size),
+                    size=np.int64(size), capacity=np.int64(capacity), pages=np.asarray(pages, dtype=np.int64),
+                    raised=np.bool_(raised),
+                    counts=np.asarray(list(shadow.migration_counts.values()), dtype=np.int64))
+        for layer in range(n_layers):
+            k, v, initialized = shadow.layers[10 + layer]
+            case[f"k_shadow{layer}"] = _i16(k)
+            case[f"v_shadow{layer}"] = _i16(v)
+            case[f"initialized{layer}"] = initialized.numpy()
+            case[f"pool_k{layer}"] = _i16(pool_k[layer])
+            case[f"pool_v{layer}"] = _i16(pool_v[layer])
+        cases[name] = case
+    return cases
+
+
 def main():
     ref = _import_reference()
     np.savez_compressed(HERE / "lookup_golden.npz",
@@ -314,6 +452,9 @@ def main():
                            for key, value in arrays.items()})
     np.savez_compressed(HERE / "shared_prefix_golden.npz",
                         **{f"{case}__{key}": value for case, arrays in shared_prefix_cases(ref).items()
+                           for key, value in arrays.items()})
+    np.savez_compressed(HERE / "shadow_golden.npz",
+                        **{f"{case}__{key}": value for case, arrays in shadow_cases(ref).items()
                            for key, value in arrays.items()})
     (HERE / "host_golden.json").write_text(json.dumps(
         dict(layouts=layout_cases(ref), releasable=releasable_cases(ref),

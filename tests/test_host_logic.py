@@ -480,3 +480,43 @@ def test_shared_resolvers_reject_like_the_reference():
     # A CPU tensor reaching the kernel path is refused: there is no CPU fallback.
     with pytest.raises(ValueError, match="CUDA tensor"):
         resolve_shared_block_locations_batched(torch.tensor([[0]]), source_rows=[0], shared_tokens=[2], **batched)
+
+
+# ---------------------------------------------------------------- logical shadow (host side)
+
+def test_logical_shadow_host_contract(tmp_path):
+    """Errors raised before any device work and the publish record
+    (adaptive_sparse/logical_shadow.py:30-48, :88-105, :125-140)."""
+    from ekv_b200.logical_shadow import LogicalShadow
+
+    shadow = LogicalShadow(16, "cpu")
+    key = torch.zeros((2, 1, 4), dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="unit-scale BF16"):
+        shadow.write(0, torch.tensor([1, 2]), key.float(), key, (None, None))
+    with pytest.raises(RuntimeError, match="unit-scale BF16"):
+        shadow.write(0, torch.tensor([1, 2]), key, key, (None, 0.5))
+    with pytest.raises(RuntimeError, match="recorded producer writes"):
+        shadow.check(5, key, key, None, None, None, 1, torch.zeros((1, 1, 1), dtype=torch.int32), None, None, 1)
+    with pytest.raises(ValueError, match="Invalid migration shadow slot vectors"):
+        shadow.check_complete(None, torch.zeros((2, 2)), torch.zeros((2, 2)), "b")
+    with pytest.raises(ValueError, match="Invalid migration shadow slot vectors"):
+        shadow.check_complete(None, torch.zeros(0), torch.zeros(0), "b")
+    pool = SimpleNamespace(page_size=4, size=64, start_layer=3, end_layer=5)
+    with pytest.raises(RuntimeError, match="Missing migration shadow writes for layer 3"):
+        shadow.check_complete(pool, torch.arange(4, 8), torch.arange(4, 8), "b")
+    shadow.reset(torch.tensor([1, 2]))  # no layers yet: nothing to do
+
+    shadow.publish(tmp_path, 0)  # not dirty: no file
+    assert not list(tmp_path.iterdir())
+    shadow.counts += torch.tensor([5, 40, 0, 0, 0, 1, 0])
+    shadow.migration_counts["migration_checked_tokens"] = 9
+    shadow.dirty = True
+    shadow.publish(tmp_path, 2)
+    stats = __import__("json").loads((tmp_path / "shadow-tp-2.json").read_text())
+    assert stats["checked_tokens"] == 5 and stats["checked_bytes"] == 40 and stats["checked_calls"] == 1
+    assert stats["migration_checked_tokens"] == 9 and stats["tp_rank"] == 2 and stats["logical_capacity"] == 16
+    assert stats["boundary"] == "scheduler_idle" and not shadow.dirty
+    shadow.counts[6] += 1  # a malformed Top-K block is a failure
+    shadow.dirty = True
+    with pytest.raises(RuntimeError, match="Logical KV shadow mismatch"):
+        shadow.publish(tmp_path, 2)

@@ -246,3 +246,36 @@ def test_shared_prefix_fixture_covers_the_edges():
     total_invalid = sum(int((~SHARED_CASES[c]["valid"]).sum()) for c in SHARED_CASES if c.startswith("random"))
     assert total_valid > 100 and total_invalid > 100
     assert any((SHARED_CASES[c]["physical"] == 77).any() for c in SHARED_CASES if c.startswith("random"))
+
+
+# --------------------------------------------------------------------------- logical shadow
+
+from oracle import logical_shadow as osh  # noqa: E402
+
+SHADOW_CASES = load_npz_cases("shadow_golden.npz")
+
+
+@pytest.mark.parametrize("case", sorted(c for c in SHADOW_CASES if c.startswith("check_")))
+def test_shadow_check_oracle_matches_reference(case):
+    c = SHADOW_CASES[case]
+    counts, clean, physical = osh.check(c["k_shadow"], c["v_shadow"], c["initialized"], c["k_cache"], c["v_cache"],
+                                        c["table"], c["lengths"], c["rows"], int(c["block_size"]), c["blocks"],
+                                        c.get("physical"), c.get("live_pages"), int(c["page_size"]))
+    np.testing.assert_array_equal(counts, c["counts"])
+    np.testing.assert_array_equal(clean, c["clean_blocks"])
+    assert clean.dtype == c["clean_blocks"].dtype
+    np.testing.assert_array_equal(physical, c["physical_out"])
+
+
+@pytest.mark.parametrize("case", sorted(c for c in SHADOW_CASES if c.startswith("complete_")))
+def test_shadow_check_complete_oracle_matches_reference(case):
+    c = SHADOW_CASES[case]
+    n_layers = sum(1 for k in c if k.startswith("pool_k"))
+    page, size = int(c["page_size"]), int(c["size"])
+    live = np.zeros(size // page + 1, dtype=bool)
+    live[c["pages"]] = True
+    counts = osh.check_complete([(c[f"k_shadow{i}"], c[f"v_shadow{i}"], c[f"initialized{i}"]) for i in range(n_layers)],
+                                [c[f"pool_k{i}"] for i in range(n_layers)], [c[f"pool_v{i}"] for i in range(n_layers)],
+                                c["logical"], c["physical"], page, size, live, int(c["capacity"]))
+    np.testing.assert_array_equal(counts, c["counts"])
+    assert bool(c["raised"]) == bool(counts[2] or counts[3])
