@@ -630,18 +630,76 @@ def shadow_bench(dist: Dist, reps: int = 10):
     ref_ms = per_call_ms(reference)
     ref_counts, ref_clean, ref_phys = reference()
     clean, phys_out = ours()
-    agree = bool(torch.equal(ref_clean, clean)) and bool(torch.equal(ref_phys, phys_out))
     calls = counts[5]
+    agree = (bool(torch.equal(ref_clean, clean)) and bool(torch.equal(ref_phys, phys_out))
+             and calls > 0 and ref_counts.tolist()[0] == counts[0] / calls)
     row_bytes = heads * dim * 2
     per_token = 4 * row_bytes + 17
     achieved = batch * topk * per_token / (ours_ms * 1e-3) / 1e9
     peak, source = measured_hbm_peak()
-    return {"shape": f"{batch} x {topk} tokens, {row_bytes} B rows, {capacity}-slot shadow and cache",
-            "check_ms": ours_ms, "tokens_per_s": batch * topk / (ours_ms * 1e-3),
-            "achieved_gbs": achieved, "peak_gbs": peak, "frac": achieved / peak, "peak_source": source,
-            "reference_torch_same_gpu_ms": ref_ms, "speedup_vs_reference_torch": ref_ms / ours_ms,
-            "checked_per_call": counts[0] / calls if calls else 0, "mismatched": counts[4],
-            "agrees_with_reference_torch": agree and ref_counts.tolist()[0] == counts[0] / calls}
+    del k_cache, v_cache, table, physical, blocks, args, ref_counts, ref_clean, ref_phys
+    result = {"shape": f"{batch} x {topk} tokens, {row_bytes} B rows, {capacity}-slot shadow and cache",
+              "check_ms": ours_ms, "tokens_per_s": batch * topk / (ours_ms * 1e-3),
+              "achieved_gbs": achieved, "peak_gbs": peak, "frac": achieved / peak, "peak_source": source,
+              "reference_torch_same_gpu_ms": ref_ms, "speedup_vs_reference_torch": ref_ms / ours_ms,
+              "checked_per_call": counts[0] / calls if calls else 0, "mismatched": counts[4],
+              "agrees_with_reference_torch": agree}
+    result["migration_check"] = shadow_complete_bench(shadow, dev, heads, dim, capacity, reps)
+    return result
+
+
+def shadow_complete_bench(shadow, dev, heads, dim, capacity, reps, layers=4, pairs=196608):
+    """check_complete after a config-3-sized migration (196608 slot pairs) over 4
+    layers, each with its own shadow and pool buffers (1 GiB each): per pair and
+    layer the pool's K and V rows and the shadow's (4 x 2 KiB) + 16 B of slot ids."""
+    from types import SimpleNamespace
+
+    gen = torch.Generator(device=dev).manual_seed(6)
+    page = 1
+    key0, value0, init0 = shadow.layers[0]
+    for layer in range(1, layers):  # the same recorded writes, in each layer's own buffers
+        shadow.layers[layer] = (key0.clone(), value0.clone(), init0.clone())
+    logical = torch.randperm(capacity - page, device=dev, generator=gen)[:pairs] + page
+    physical = torch.randperm(capacity, device=dev, generator=gen)[:pairs] + page
+    pool_k, pool_v = [], []
+    for layer in range(layers):
+        pk = torch.empty((capacity + page, heads, dim), device=dev, dtype=torch.bfloat16)
+        pv = torch.empty_like(pk)
+        pk[physical], pv[physical] = key0[logical], value0[logical]
+        pool_k.append(pk)
+        pool_v.append(pv)
+    pool = SimpleNamespace(page_size=page, size=capacity, adaptive_vmm=SimpleNamespace(pages=set(range(capacity + 1))),
+                           start_layer=0, end_layer=layers, get_key_buffer=lambda layer: pool_k[layer],
+                           get_value_buffer=lambda layer: pool_v[layer])
+    shadow.check_complete(pool, logical, physical, "bench")
+    torch.cuda.synchronize()
+    api = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        shadow.check_complete(pool, logical, physical, "bench")  # ends with the counters' host read
+        api.append((time.perf_counter() - t0) * 1e3)
+    live = torch.ones(capacity // page + 1, dtype=torch.uint8, device=dev)
+    counts = torch.zeros(4, dtype=torch.int64, device=dev)
+    layer_ids = list(range(layers))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(reps):
+        shadow.launch_complete(pool, layer_ids, logical, physical, live, counts)
+    end.record()
+    end.synchronize()
+    ms = start.elapsed_time(end) / reps
+    row_bytes = heads * dim * 2
+    moved = pairs * layers * (4 * row_bytes + 16)
+    peak, _ = measured_hbm_peak()
+    checked = shadow.migration_counts["migration_checked_tokens"]
+    return {"pairs": pairs, "layers": layers, "kernel_ms": ms, "achieved_gbs": moved / (ms * 1e-3) / 1e9,
+            "frac": moved / (ms * 1e-3) / 1e9 / peak, "api_ms_p50": statistics.median(api),
+            "checked_all": checked == pairs * layers * (reps + 1) and int(counts[0]) == pairs * layers * reps,
+            "mismatched": shadow.migration_counts["migration_mismatched_tokens"] + int(counts[3]),
+            "timing": "kernel_ms: CUDA events around the launches alone; api_ms_p50: wall time of the public "
+                      "call (live-page mask from the page set, launch, counter read)"}
+
 
 
 # --------------------------------------------------------------------------- bitmap (config 4 geometry)

@@ -60,14 +60,39 @@ __device__ __forceinline__ bool rows_differ(const char* a, const char* b, int64_
     return differ;
 }
 
-__device__ __forceinline__ bool rows_differ_any(const char* a, const char* b, int64_t row_bytes, int vec,
-                                                unsigned lane) {
-    switch (vec) {
-        case 16: return rows_differ<uint4>(a, b, row_bytes, lane);
-        case 8: return rows_differ<unsigned long long>(a, b, row_bytes, lane);
-        case 4: return rows_differ<unsigned int>(a, b, row_bytes, lane);
-        default: return rows_differ<unsigned short>(a, b, row_bytes, lane);
+// K and V rows of one token compared in ONE loop, so all of a lane's loads of
+// both row pairs are in flight together (one memory round trip per token for
+// rows up to 4 vectors per lane).  Requires equal K and V row lengths.
+template <class V>
+__device__ __forceinline__ bool row_pairs_differ(const char* ka, const char* kb, const char* va, const char* vb,
+                                                 int64_t row_bytes, unsigned lane) {
+    const int64_t n = row_bytes / static_cast<int64_t>(sizeof(V));
+    const V* k0 = reinterpret_cast<const V*>(ka);
+    const V* k1 = reinterpret_cast<const V*>(kb);
+    const V* v0 = reinterpret_cast<const V*>(va);
+    const V* v1 = reinterpret_cast<const V*>(vb);
+    bool differ = false;
+#pragma unroll 4
+    for (int64_t i = lane; i < n; i += 32) {
+        const V a = __ldg(k0 + i);
+        const V b = __ldg(k1 + i);
+        const V c = __ldg(v0 + i);
+        const V d = __ldg(v1 + i);
+        if constexpr (sizeof(V) == 16) {
+            differ |= (a.x != b.x) | (a.y != b.y) | (a.z != b.z) | (a.w != b.w) | (c.x != d.x) | (c.y != d.y) |
+                      (c.z != d.z) | (c.w != d.w);
+        } else {
+            differ |= (a != b) | (c != d);
+        }
     }
+    return differ;
+}
+
+template <class V>
+__device__ __forceinline__ bool kv_differ(const char* ka, const char* kb, int64_t k_bytes, const char* va,
+                                          const char* vb, int64_t v_bytes, unsigned lane) {
+    if (k_bytes == v_bytes) return row_pairs_differ<V>(ka, kb, va, vb, k_bytes, lane);
+    return rows_differ<V>(ka, kb, k_bytes, lane) | rows_differ<V>(va, vb, v_bytes, lane);
 }
 
 __device__ __forceinline__ void add_counts(unsigned long long* counts, const unsigned (&local)[5],
@@ -106,7 +131,11 @@ struct CheckParams {
     int vec;
 };
 
-__global__ void __launch_bounds__(kShadowThreads)
+// 2 blocks per SM leave 128 registers a thread: room for all 16 row vectors a
+// lane loads per token (K and V, cache and shadow, 2 KiB rows) to be in flight
+// at once (16 warps x 8 KiB per SM is far more than HBM latency needs).
+template <class V>
+__global__ void __launch_bounds__(kShadowThreads, 2)
 shadow_check_kernel(const __grid_constant__ CheckParams p) {
     __shared__ int first_invalid;
     __shared__ unsigned block_sum[5];  // checked, uninitialized, invalid physical, mismatched, malformed
@@ -195,10 +224,9 @@ shadow_check_kernel(const __grid_constant__ CheckParams p) {
             const int64_t s = __shfl_sync(0xffffffffu, safe, src);
             const int64_t l = __shfl_sync(0xffffffffu, logical, src);
             const bool differ =
-                rows_differ_any(p.k_cache + s * p.k_cache_stride, p.k_shadow + l * p.k_shadow_stride,
-                                p.k_row_bytes, p.vec, lane) |
-                rows_differ_any(p.v_cache + s * p.v_cache_stride, p.v_shadow + l * p.v_shadow_stride,
-                                p.v_row_bytes, p.vec, lane);
+                kv_differ<V>(p.k_cache + s * p.k_cache_stride, p.k_shadow + l * p.k_shadow_stride, p.k_row_bytes,
+                             p.v_cache + s * p.v_cache_stride, p.v_shadow + l * p.v_shadow_stride, p.v_row_bytes,
+                             lane);
             if (__any_sync(0xffffffffu, differ) && lane == static_cast<unsigned>(src)) local[3] += 1u;
         }
     }
@@ -222,7 +250,7 @@ struct CompleteParams {
     const void* physical;
     const uint8_t* live;
     unsigned long long* counts;
-    int64_t n, page_size, pool_size, capacity, live_len;
+    int64_t n, page_size, pool_size, capacity, live_len, tile;
     int64_t pool_k_stride, pool_v_stride, shadow_k_stride, shadow_v_stride;
     int64_t k_row_bytes, v_row_bytes;
     int logical_es, physical_es, vec, n_layers;
@@ -234,7 +262,8 @@ struct CompleteParams {
 };
 
 // grid.x tiles the slot pairs, grid.y walks the layers.
-__global__ void __launch_bounds__(kShadowThreads)
+template <class V>
+__global__ void __launch_bounds__(kShadowThreads, 2)
 shadow_complete_kernel(const __grid_constant__ CompleteParams p) {
     __shared__ unsigned block_sum[5];
     const unsigned lane = lane_id();
@@ -243,8 +272,8 @@ shadow_complete_kernel(const __grid_constant__ CompleteParams p) {
     __syncthreads();
     unsigned local[5] = {0, 0, 0, 0, 0};  // checked, invalid, mismatched
     for (int layer = blockIdx.y; layer < p.n_layers; layer += gridDim.y) {
-        const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kShadowTokensPerBlock;
-        const int64_t i1 = min(p.n, i0 + kShadowTokensPerBlock);
+        const int64_t i0 = static_cast<int64_t>(blockIdx.x) * p.tile;
+        const int64_t i1 = min(p.n, i0 + p.tile);
         for (int64_t base = i0 + static_cast<int64_t>(warp) * 32; base < i1; base += kShadowThreads) {
             const int64_t i = base + lane;
             bool valid = false;
@@ -270,10 +299,9 @@ shadow_complete_kernel(const __grid_constant__ CompleteParams p) {
                 const int64_t s = __shfl_sync(0xffffffffu, sp, src);
                 const int64_t l = __shfl_sync(0xffffffffu, sl, src);
                 const bool differ =
-                    rows_differ_any(p.pool_k[layer] + s * p.pool_k_stride, p.shadow_k[layer] + l * p.shadow_k_stride,
-                                    p.k_row_bytes, p.vec, lane) |
-                    rows_differ_any(p.pool_v[layer] + s * p.pool_v_stride, p.shadow_v[layer] + l * p.shadow_v_stride,
-                                    p.v_row_bytes, p.vec, lane);
+                    kv_differ<V>(p.pool_k[layer] + s * p.pool_k_stride, p.shadow_k[layer] + l * p.shadow_k_stride,
+                                 p.k_row_bytes, p.pool_v[layer] + s * p.pool_v_stride,
+                                 p.shadow_v[layer] + l * p.shadow_v_stride, p.v_row_bytes, lane);
                 if (__any_sync(0xffffffffu, differ) && lane == static_cast<unsigned>(src)) local[2] += 1u;
             }
         }
@@ -309,18 +337,10 @@ __device__ __forceinline__ void copy_row(char* dst, const char* src, int64_t row
     for (int64_t i = lane; i < n; i += 32) reinterpret_cast<V*>(dst)[i] = __ldg(reinterpret_cast<const V*>(src) + i);
 }
 
-__device__ __forceinline__ void copy_row_any(char* dst, const char* src, int64_t row_bytes, int vec, unsigned lane) {
-    switch (vec) {
-        case 16: copy_row<uint4>(dst, src, row_bytes, lane); break;
-        case 8: copy_row<unsigned long long>(dst, src, row_bytes, lane); break;
-        case 4: copy_row<unsigned int>(dst, src, row_bytes, lane); break;
-        default: copy_row<unsigned short>(dst, src, row_bytes, lane); break;
-    }
-}
-
 // One warp per written row; slots outside [-capacity, capacity) are skipped,
 // negative ones count from the end (Python indexing, as the reference's
 // tensor assignment does).
+template <class V>
 __global__ void __launch_bounds__(kShadowThreads)
 shadow_write_kernel(const __grid_constant__ WriteParams p) {
     const unsigned lane = lane_id();
@@ -329,9 +349,8 @@ shadow_write_kernel(const __grid_constant__ WriteParams p) {
         int64_t slot = load_index(p.locations, p.loc_es, r);
         if (slot < 0) slot += p.capacity;
         if (slot < 0 || slot >= p.capacity) continue;
-        copy_row_any(p.k_shadow + slot * p.k_shadow_stride, p.key + r * p.key_stride, p.k_row_bytes, p.vec, lane);
-        copy_row_any(p.v_shadow + slot * p.v_shadow_stride, p.value + r * p.value_stride, p.v_row_bytes, p.vec,
-                     lane);
+        copy_row<V>(p.k_shadow + slot * p.k_shadow_stride, p.key + r * p.key_stride, p.k_row_bytes, lane);
+        copy_row<V>(p.v_shadow + slot * p.v_shadow_stride, p.value + r * p.value_stride, p.v_row_bytes, lane);
         if (lane == 0) p.initialized[slot] = 1;
     }
 }
@@ -362,6 +381,24 @@ int vector_width(std::initializer_list<uint64_t> values) {
         if ((bits & static_cast<uint64_t>(w - 1)) == 0) return w;
     }
     return 2;
+}
+
+// Call f(V{}) with V the unsigned type of `vec` bytes.
+template <class F>
+void with_vector(int vec, F&& f) {
+    switch (vec) {
+        case 16: f(uint4{}); break;
+        case 8: f(static_cast<unsigned long long>(0)); break;
+        case 4: f(0u); break;
+        default: f(static_cast<unsigned short>(0)); break;
+    }
+}
+
+// Token tile per block so the grid covers every SM a few times over.
+int64_t tokens_per_block(int64_t tokens, int device) {
+    const int64_t target = static_cast<int64_t>(sm_count(device)) * 2;
+    const int64_t per = (tokens + target - 1) / target;
+    return std::max<int64_t>(64, std::min<int64_t>(kShadowTokensPerBlock, per));
 }
 
 int grid_for(int64_t work, int64_t per_block, int device) {
@@ -442,8 +479,8 @@ extern "C" int ekv_shadow_check(
         p.len_es = len_esize;
         p.rows_es = rows_esize;
         p.table_es = table_esize;
-        p.blocks_per_cta = std::max<int64_t>(1, std::min<int64_t>(n_blocks, kShadowTokensPerBlock / block_size));
-        if (p.blocks_per_cta > kShadowTokensPerBlock) p.blocks_per_cta = kShadowTokensPerBlock;
+        const int64_t tile = tokens_per_block(batch * n_blocks * block_size, device);
+        p.blocks_per_cta = std::max<int64_t>(1, std::min<int64_t>(n_blocks, tile / block_size));
         p.vec = vector_width({reinterpret_cast<uint64_t>(k_cache), reinterpret_cast<uint64_t>(v_cache),
                               reinterpret_cast<uint64_t>(k_shadow), reinterpret_cast<uint64_t>(v_shadow),
                               static_cast<uint64_t>(k_cache_stride), static_cast<uint64_t>(v_cache_stride),
@@ -452,7 +489,9 @@ extern "C" int ekv_shadow_check(
         const int64_t x = n_blocks > 0 ? (n_blocks + p.blocks_per_cta - 1) / p.blocks_per_cta : 1;
         require(x <= 0x7fffffff, "grid too large");
         const dim3 grid(static_cast<unsigned>(x), static_cast<unsigned>(std::max<int64_t>(1, p.batch)));
-        shadow_check_kernel<<<grid, kShadowThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        with_vector(p.vec, [&](auto v) {
+            shadow_check_kernel<decltype(v)><<<grid, kShadowThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        });
         check_launch("shadow_check launch");
     });
 }
@@ -509,10 +548,13 @@ extern "C" int ekv_shadow_check_complete(
             bits |= pool_k[l] | pool_v[l] | shadow_k[l] | shadow_v[l];
         }
         p.vec = vector_width({bits});
-        const int64_t x = (n + kShadowTokensPerBlock - 1) / kShadowTokensPerBlock;
+        p.tile = tokens_per_block(n * n_layers, device);
+        const int64_t x = (n + p.tile - 1) / p.tile;
         require(x <= 0x7fffffff, "grid too large");
         const dim3 grid(static_cast<unsigned>(x), static_cast<unsigned>(std::min(n_layers, 65535)));
-        shadow_complete_kernel<<<grid, kShadowThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        with_vector(p.vec, [&](auto v) {
+            shadow_complete_kernel<decltype(v)><<<grid, kShadowThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        });
         check_launch("shadow_check_complete launch");
     });
 }
@@ -552,8 +594,10 @@ extern "C" int ekv_shadow_write(
                               static_cast<uint64_t>(k_shadow_stride), static_cast<uint64_t>(v_shadow_stride),
                               static_cast<uint64_t>(key_stride), static_cast<uint64_t>(value_stride),
                               static_cast<uint64_t>(k_row_bytes), static_cast<uint64_t>(v_row_bytes)});
-        shadow_write_kernel<<<grid_for(n, kShadowWarps, device), kShadowThreads, 0,
-                              static_cast<cudaStream_t>(stream)>>>(p);
+        with_vector(p.vec, [&](auto v) {
+            shadow_write_kernel<decltype(v)><<<grid_for(n, kShadowWarps, device), kShadowThreads, 0,
+                                               static_cast<cudaStream_t>(stream)>>>(p);
+        });
         check_launch("shadow_write launch");
     });
 }

@@ -173,12 +173,26 @@ class LogicalShadow:
             if layer not in self.layers:
                 raise RuntimeError(f"Missing migration shadow writes for layer {layer}")
         device = torch.device(self.device)
+        # The live-page mask: a scatter, so the page set needs no sorting.
+        pages = pool.adaptive_vmm.pages
         live_host = np.zeros(pool.size // page + 1, dtype=np.uint8)
-        live_host[np.asarray(sorted(pool.adaptive_vmm.pages), dtype=np.int64)] = 1
+        live_host[np.fromiter(pages, dtype=np.int64, count=len(pages))] = 1
         live = torch.from_numpy(live_host).to(device)
-        logical_t = _index(logical, device)
-        physical_t = _index(physical, device)
         counts = torch.zeros(4, device=device, dtype=torch.int64)
+        self.launch_complete(pool, layers, _index(logical, device), _index(physical, device), live, counts)
+        report = dict(zip(self.migration_counts, counts.tolist(), strict=True))
+        for name, count in report.items():
+            self.migration_counts[name] += count
+        self.dirty = True
+        if report["migration_invalid_tokens"] or report["migration_mismatched_tokens"]:
+            raise RuntimeError(f"Logical KV migration shadow mismatch at {boundary}: {report}")
+
+    def launch_complete(self, pool, layers, logical, physical, live, counts):
+        """The device part of ``check_complete``: ADD the four migration counters of
+        ``layers`` to ``counts`` (int64 [4] on the device) without synchronizing.
+        ``live`` is the uint8 live-page mask [pool.size // page_size + 1]."""
+        page = pool.page_size
+        device = torch.device(self.device)
         groups: dict[tuple, list] = {}
         for layer in layers:
             key, value, initialized = self.layers[layer]
@@ -198,17 +212,11 @@ class LogicalShadow:
                 part = members[start:start + SHADOW_MAX_LAYERS]
                 columns = list(zip(*part))
                 call("ekv_shadow_check_complete",
-                     logical_t.data_ptr(), index_esize(logical_t, "logical"),
-                     physical_t.data_ptr(), index_esize(physical_t, "physical"), logical_t.numel(),
+                     logical.data_ptr(), index_esize(logical, "logical"),
+                     physical.data_ptr(), index_esize(physical, "physical"), logical.numel(),
                      page, pool.size, self.capacity, live.data_ptr(), live.numel(),
                      *(u64_array(c) for c in columns), len(part), pks, pvs, sks, svs, kb, vb,
                      counts.data_ptr(), device.index, stream_handle(device))
-        report = dict(zip(self.migration_counts, counts.tolist(), strict=True))
-        for name, count in report.items():
-            self.migration_counts[name] += count
-        self.dirty = True
-        if report["migration_invalid_tokens"] or report["migration_mismatched_tokens"]:
-            raise RuntimeError(f"Logical KV migration shadow mismatch at {boundary}: {report}")
 
     def publish(self, directory, rank):
         """Write shadow-tp-<rank>.json and raise on any mismatch (logical_shadow.py:125-140)."""
