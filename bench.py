@@ -405,6 +405,7 @@ def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
     pack_rows(planes, dst, restored, plane_index=plane_index, stage_rows=dense)
     torch.cuda.synchronize()
     exact = bool(torch.equal(restored, shadow))
+    commit = commit_path_bench(work, victims, segments, planes, dst, host, plane_index, shadow, dense)
     # Copy-engine reference on the same link: one contiguous pinned <-> device copy.
     flat_host = host[:moved]
     flat_dev = torch.empty(moved, dtype=torch.uint8, device=dev)
@@ -420,13 +421,89 @@ def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
             "host_link_nominal_gbs": 64.0, "frac_of_nominal_d2h": gbs(d2h_best) / 64.0,
             "frac_of_nominal_h2d": gbs(h2d_best) / 64.0,
             "reclaim_ms": reclaim_s * 1e3, "ensure_ms": ensure_s * 1e3,
-            "round_trip_bit_exact": exact,
+            "round_trip_bit_exact": exact, "commit_path": commit,
             "path": "staged: pack/unpack kernel into a 64 MiB device ring + copy-engine transfers on a side "
                     "stream, dense host layout (2 MiB pinned chunks, victim start rows recorded); "
                     "alternatives: per-victim 2 MiB-aligned host layout, zero-copy kernel stores/loads"}
 
 
 # --------------------------------------------------------------------------- lookups (config 1, R1)
+
+def commit_path_bench(work, victims, segments, planes, dst, host, plane_index, shadow, dense, batch=32,
+                      rounds=3):
+    """Promotion into freshly committed chunks (config 3): the 256 victim chunks are
+    reclaimed, then committed again and their rows restored from pinned host memory.
+
+    * sequential: commit every chunk, then restore every row (the reference's order:
+      the allocator maps, then load_to_device_per_layer copies);
+    * pipelined: commit 32 victims' chunks, launch their rows' restore (asynchronous:
+      copy engine + unpack kernel), commit the next 32 while it runs;
+    * *_spare_handles: the same after a reclaim that kept the physical handles (no
+      cuMemRelease / cuMemCreate).
+    Wall time from the first commit to the restored rows on the device, min and median
+    of 3 interleaved rounds; every run is checked bit for bit against the rows before
+    demotion."""
+    from ekv_b200.host_pool import pack_rows, pack_rows_staged, unpack_rows_staged
+
+    chunk_of = [1 + int(v) for v in victims]
+    firsts = [first for first, _, _ in segments] + [dst.numel()]
+    row_bytes = work.row_bytes
+    # The dense host image of the restored rows (victim v's rows from row firsts[v]).
+    pack_rows_staged(planes, dst, host, [(0, dst.numel(), 0)], plane_index=plane_index)
+
+    def restore(a, b):
+        first, last = firsts[a], firsts[b]
+        unpack_rows_staged(planes, dst[first:last], host, [(0, last - first, first * row_bytes)],
+                           plane_index=plane_index[first:last])
+
+    def exact():
+        restored = torch.empty_like(shadow)
+        pack_rows(planes, dst, restored, plane_index=plane_index, stage_rows=dense)
+        torch.cuda.synchronize()
+        return bool(torch.equal(restored, shadow))
+
+    def run(pipelined):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        if pipelined:
+            for a in range(0, len(chunk_of), batch):
+                b = min(len(chunk_of), a + batch)
+                work.backing.ensure(chunk_of[a:b])
+                restore(a, b)
+        else:
+            work.backing.ensure(chunk_of)
+            restore(0, len(chunk_of))
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) * 1e3
+
+    variants = (("sequential", False, 0), ("pipelined", True, 0),
+                ("sequential_spare_handles", False, len(chunk_of)),
+                ("pipelined_spare_handles", True, len(chunk_of)))
+    samples = {name: {"reclaim_ms": [], "commit_and_restore_ms": [], "bit_exact": True} for name, _, _ in variants}
+    for _ in range(rounds):  # interleaved: the driver's cost drifts between calls
+        for name, pipelined, spare in variants:
+            work.backing.set_spare_chunks(spare)
+            t0 = time.perf_counter()
+            work.backing.reclaim(chunk_of)
+            samples[name]["reclaim_ms"].append((time.perf_counter() - t0) * 1e3)
+            samples[name]["commit_and_restore_ms"].append(run(pipelined))
+            samples[name]["bit_exact"] &= exact()
+    work.backing.set_spare_chunks(0)
+    out = {name: {"reclaim_ms_min": min(v["reclaim_ms"]), "reclaim_ms_median": statistics.median(v["reclaim_ms"]),
+                  "commit_and_restore_ms_min": min(v["commit_and_restore_ms"]),
+                  "commit_and_restore_ms_median": statistics.median(v["commit_and_restore_ms"]),
+                  "bit_exact": v["bit_exact"]} for name, v in samples.items()}
+    restore_only = []
+    for _ in range(2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        restore(0, len(chunk_of))
+        torch.cuda.synchronize()
+        restore_only.append((time.perf_counter() - t0) * 1e3)
+    out["restore_only_ms"] = min(restore_only)
+    out["chunks"] = len(chunk_of)
+    return out
+
 
 def lookup_bench(dist: Dist, rounds: int = 20, calls: int = 100):
     """R2 at config 1 and R1 at the reference's own microbenchmark shape.

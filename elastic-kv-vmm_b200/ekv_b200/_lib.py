@@ -171,6 +171,8 @@ _VMM = {
     "ev_granularity": ([_p], ct.c_uint64),
     "ev_poisoned": ([_p], ct.c_int),
     "ev_close": ([_p], ct.c_int),
+    "ev_set_spare": ([_p, ct.c_uint64], ct.c_int),
+    "ev_spare": ([_p], ct.c_uint64),
     "ev_error": ([], ct.c_char_p),
 }
 

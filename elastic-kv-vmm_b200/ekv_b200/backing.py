@@ -56,7 +56,8 @@ class Backing:
     chunk until it is ensured again.
     """
 
-    def __init__(self, capacity_bytes, chunk_bytes=DEFAULT_CHUNK_BYTES, device=0, library=None):
+    def __init__(self, capacity_bytes, chunk_bytes=DEFAULT_CHUNK_BYTES, device=0, library=None, *,
+                 spare_chunks=0):
         self.capacity_bytes = operator.index(capacity_bytes)
         self.chunk_bytes = operator.index(chunk_bytes)
         if not (0 < self.capacity_bytes < _INVALID and 0 < self.chunk_bytes < _INVALID):
@@ -88,6 +89,8 @@ class Backing:
             ("ensure_calls", "ensure_chunks", "ensure_ns", "precommit_calls", "precommit_chunks",
              "precommit_ns", "reclaim_calls", "reclaim_chunks", "reclaim_ns", "reclaim_sync_ns",
              "peak_backed_bytes"), 0)
+        if spare_chunks:
+            self.set_spare_chunks(spare_chunks)
 
     @property
     def _handle(self):
@@ -133,9 +136,31 @@ class Backing:
         return self._number("ev_backed")
 
     @property
+    def spare_bytes(self):
+        """Device memory held by unmapped physical handles kept for reuse."""
+        return self._number("ev_spare")
+
+    def set_spare_chunks(self, chunks):
+        """Keep up to ``chunks`` physical handles that ``reclaim`` unmaps, so a later
+        ``ensure`` maps them again instead of creating new ones (skips cuMemRelease +
+        cuMemCreate, ~300 us per 2 MiB chunk on B200).  0 (the default, the
+        reference's behaviour) releases every reclaimed chunk at once; lowering
+        the limit releases the surplus now.  Kept handles are device memory that
+        ``backed_bytes`` does not count."""
+        self._check()
+        chunks = operator.index(chunks)
+        if chunks < 0:
+            raise ValueError("spare chunk limit must be non-negative")
+        if self._lib.ev_set_spare(self._handle, chunks):
+            error = self._error()
+            if self._lib.ev_poisoned(self._handle) != 0:
+                self._poisoned = True
+            raise RuntimeError(error)
+
+    @property
     def metrics(self):
         return {**self._metrics, "backed_bytes": self.backed_bytes,
-                "reserved_bytes": self.reserved_bytes}
+                "reserved_bytes": self.reserved_bytes, "spare_bytes": self.spare_bytes}
 
     @property
     def raw(self):

@@ -27,6 +27,15 @@
  *                 later mutating call fails), 0 otherwise, -1 on error.
  *   ev_close      synchronize the context, release everything, free the handle.
  *   ev_error      thread-local message of the last failure.
+ *
+ * Additions without a reference counterpart (the reference behaviour is the
+ * default, a spare limit of 0):
+ *   ev_set_spare  keep up to `chunks` physical handles that ev_drop unmaps, for
+ *                 ev_ensure / ev_precommit to map again instead of creating new
+ *                 ones (on B200 cuMemRelease + cuMemCreate cost ~300 us per 2 MiB
+ *                 chunk); lowering the limit releases the surplus now.  Kept
+ *                 handles hold device memory but are not counted by ev_backed.
+ *   ev_spare      bytes held by kept handles; UINT64_MAX on error.
  */
 #ifndef EKV_VMM_H
 #define EKV_VMM_H
@@ -57,6 +66,9 @@ int ev_poisoned(void* handle);
 const char* ev_error(void);
 /* native/elastic_vmm.cpp:359 */
 int ev_close(void* handle);
+/* no reference counterpart (see above) */
+int ev_set_spare(void* handle, uint64_t chunks);
+uint64_t ev_spare(void* handle);
 
 #ifdef __cplusplus
 }

@@ -82,3 +82,36 @@ def test_reference_ctypes_binding_loads_this_library(cuda_device, library_path):
     assert lib.ev_poisoned(handle) == 0
     assert lib.ev_drop(handle, ids, 2) == 0 and lib.ev_backed(handle) == 0
     assert lib.ev_close(handle) == 0
+
+
+def test_spare_handles_are_reused_and_zeroed(cuda_device):
+    """Reclaimed physical handles kept under the spare limit come back through the next
+    ensure: the chunk reads as zeros again (the zero fill runs for reused handles too),
+    spare memory is reported apart from the backed bytes, and lowering the limit or
+    closing releases it."""
+    from ekv_b200.backing import Backing
+
+    backing = Backing(16 * CHUNK, CHUNK, device=cuda_device.index, spare_chunks=3)
+    try:
+        assert backing.ensure({0, 1, 2, 3, 4}) == 5
+        raw = backing.raw
+        raw[CHUNK:5 * CHUNK].fill_(0x5A)
+        torch.cuda.synchronize()
+        assert backing.reclaim({1, 2, 3, 4}) == 4
+        assert backing.spare_bytes == 3 * CHUNK and backing.backed_bytes == CHUNK
+        assert backing.ensure({9, 10}) == 2
+        assert backing.spare_bytes == CHUNK and backing.backed_bytes == 3 * CHUNK
+        assert not raw[9 * CHUNK:11 * CHUNK].any()  # reused handles are zero-filled
+        raw[9 * CHUNK:11 * CHUNK].fill_(7)
+        torch.cuda.synchronize()
+        assert int(raw[10 * CHUNK + 5]) == 7
+        assert backing.metrics["spare_bytes"] == CHUNK
+        backing.set_spare_chunks(0)
+        assert backing.spare_bytes == 0
+        assert backing.ensure({12}) == 1 and not raw[12 * CHUNK:13 * CHUNK].any()
+        backing.set_spare_chunks(8)
+        assert backing.reclaim({9, 10, 12}) == 3 and backing.spare_bytes == 3 * CHUNK
+        del raw
+    finally:
+        torch.cuda.synchronize()
+        backing.close()  # releases the kept handles too

@@ -197,6 +197,8 @@ class FakeLibrary:
         self.poisoned = 0
         self.error = b""
         self.mapped = set()
+        self.spare_limit = 0
+        self.spare = 0
 
     def ev_create(self, device, capacity, chunk):
         self.chunk = chunk
@@ -213,10 +215,26 @@ class FakeLibrary:
             self.error = f"{name} failed".encode()
             return -1
         if name == "ev_drop":
+            dropped = len(self.mapped & set(ids))
             self.mapped.difference_update(ids)
+            self.spare = min(self.spare_limit, self.spare + dropped)
         else:
+            fresh = len(set(ids) - self.mapped)
+            self.spare -= min(self.spare, fresh)
             self.mapped.update(ids)
         return 0
+
+    def ev_set_spare(self, handle, chunks):
+        self.calls.append(("ev_set_spare", [chunks]))
+        if self.fail == "ev_set_spare":
+            self.error = b"ev_set_spare failed"
+            return -1
+        self.spare_limit = chunks
+        self.spare = min(self.spare, chunks)
+        return 0
+
+    def ev_spare(self, handle):
+        return self.spare * self.chunk
 
     def ev_ensure(self, handle, array, count):
         return self._op("ev_ensure", handle, array, count)
@@ -285,6 +303,26 @@ def test_backing_clean_failure_stays_usable_and_poison_stops_it():
         backing.reclaim({1}, synchronize=False)
     with pytest.raises(RuntimeError, match="closed or has encountered"):
         backing.ensure({2})
+
+
+def test_backing_spare_handles():
+    """Reclaimed handles are kept up to the spare limit and reused by the next ensure;
+    the metrics report them apart from the backed bytes."""
+    lib = FakeLibrary()
+    backing = Backing(16 << 20, 2 << 20, device=0, library=lib, spare_chunks=2)
+    assert lib.calls[0] == ("ev_set_spare", [2])
+    backing.ensure({1, 2, 3})
+    backing.reclaim({1, 2, 3}, synchronize=False)
+    assert backing.spare_bytes == 2 * (2 << 20) and backing.backed_bytes == 0
+    backing.ensure({4})
+    assert backing.metrics["spare_bytes"] == 2 << 20 and backing.metrics["backed_bytes"] == 2 << 20
+    backing.set_spare_chunks(0)
+    assert backing.spare_bytes == 0
+    with pytest.raises(ValueError):
+        backing.set_spare_chunks(-1)
+    lib.fail = "ev_set_spare"
+    with pytest.raises(RuntimeError, match="ev_set_spare failed"):
+        backing.set_spare_chunks(3)
 
 
 def test_backing_rejects_bad_arguments():
