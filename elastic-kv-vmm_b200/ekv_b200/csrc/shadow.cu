@@ -3,7 +3,7 @@
 // A diagnostic shadow keeps, per layer, a copy of every K/V row a producer
 // wrote (indexed by logical slot) plus an "initialized" flag per slot.
 //
-// shadow_check_kernel (one decode step of one layer; semantics of
+// shadow_clean_kernel + shadow_tokens_kernel (one decode step of one layer; semantics of
 //   LogicalShadow.check, adaptive_sparse/logical_shadow.py:45-86): cleans the
 //   Top-K block ids (keeps each row's valid prefix, -1 elsewhere, counts
 //   malformed ids), resolves every selected position through the request
@@ -126,83 +126,99 @@ struct CheckParams {
     int64_t capacity, k_shadow_stride, v_shadow_stride;
     int64_t k_row_bytes, v_row_bytes;
     int64_t batch, n_blocks, block_size, page_size;
-    int64_t blocks_per_cta;
     int blocks_es, len_es, rows_es, table_es;
     int vec;
 };
 
+// Pass 1, one block per request row: the end of the row's valid prefix (the
+// cumulative product of block validity), the cleaned ids (-1 past the prefix)
+// and the malformed-id count.  Also counts the call.
+__global__ void __launch_bounds__(kShadowThreads)
+shadow_clean_kernel(const __grid_constant__ CheckParams p) {
+    __shared__ int first_invalid;
+    __shared__ unsigned malformed;
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&p.counts[5], 1ull);  // checked_calls
+    for (int64_t b = blockIdx.x; b < p.batch; b += gridDim.x) {
+        if (threadIdx.x == 0) {
+            first_invalid = static_cast<int>(p.n_blocks);
+            malformed = 0;
+        }
+        __syncthreads();
+        const int64_t length = load_index(p.lengths, p.len_es, b * p.len_stride);
+        const int64_t limit = floor_div(length + p.block_size - 1, p.block_size);
+        for (int64_t k = threadIdx.x; k < p.n_blocks; k += kShadowThreads) {
+            const int64_t block = load_index(p.blocks, p.blocks_es, b * p.blocks_row + k * p.blocks_col);
+            if (!(block >= 0 && block < limit)) atomicMin(&first_invalid, static_cast<int>(k));
+        }
+        __syncthreads();
+        const int64_t first = first_invalid;
+        unsigned local = 0;
+        for (int64_t k = threadIdx.x; k < p.n_blocks; k += kShadowThreads) {
+            const int64_t block = load_index(p.blocks, p.blocks_es, b * p.blocks_row + k * p.blocks_col);
+            const bool valid = block >= 0 && block < limit;
+            const bool prefix = k < first;
+            local += ((block != -1 && !valid) || (valid && !prefix)) ? 1u : 0u;
+            const int64_t c = prefix ? block : -1;
+            const int64_t at = b * p.n_blocks + k;
+            if (p.blocks_es == 8) {
+                static_cast<int64_t*>(p.clean_blocks)[at] = c;
+            } else {
+                static_cast<int32_t*>(p.clean_blocks)[at] = static_cast<int32_t>(c);
+            }
+        }
+        const unsigned total = __reduce_add_sync(0xffffffffu, local);
+        if (lane_id() == 0 && total) atomicAdd(&malformed, total);
+        __syncthreads();
+        if (threadIdx.x == 0 && malformed) atomicAdd(&p.counts[6], static_cast<unsigned long long>(malformed));
+        __syncthreads();  // the shared words are reused by the next row
+    }
+}
+
+// Pass 2, persistent: every warp takes an equal contiguous slice of all
+// (request, token) pairs, so no warp idles while another finishes (ncu showed
+// blocks of uneven tiles waiting at their barrier).  Per 32 tokens: one index
+// chain per lane, then the warp compares the rows of each checked token.
 // 2 blocks per SM leave 128 registers a thread: room for all 16 row vectors a
-// lane loads per token (K and V, cache and shadow, 2 KiB rows) to be in flight
-// at once (16 warps x 8 KiB per SM is far more than HBM latency needs).
+// lane loads per token (K and V, cache and shadow, 2 KiB rows) to be in flight.
 template <class V>
 __global__ void __launch_bounds__(kShadowThreads, 2)
-shadow_check_kernel(const __grid_constant__ CheckParams p) {
-    __shared__ int first_invalid;
-    __shared__ unsigned block_sum[5];  // checked, uninitialized, invalid physical, mismatched, malformed
-    __shared__ int64_t clean[kShadowTokensPerBlock];
+shadow_tokens_kernel(const __grid_constant__ CheckParams p) {
+    __shared__ unsigned block_sum[5];  // checked, uninitialized, invalid physical, mismatched
     const unsigned lane = lane_id();
-    const int warp = threadIdx.x >> 5;
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicAdd(&p.counts[5], 1ull);  // checked_calls
-    const int64_t b = blockIdx.y;
-    if (b >= p.batch) return;
-    if (threadIdx.x == 0) first_invalid = static_cast<int>(p.n_blocks);
     if (threadIdx.x < 5) block_sum[threadIdx.x] = 0;
     __syncthreads();
-
-    const int64_t length = load_index(p.lengths, p.len_es, b * p.len_stride);
-    const int64_t req = load_index(p.rows, p.rows_es, b * p.rows_stride);
-    const int64_t limit = floor_div(length + p.block_size - 1, p.block_size);
-    // 1. End of the row's valid prefix (the cumulative product of validity).
-    for (int64_t k = threadIdx.x; k < p.n_blocks; k += kShadowThreads) {
-        const int64_t block = load_index(p.blocks, p.blocks_es, b * p.blocks_row + k * p.blocks_col);
-        if (!(block >= 0 && block < limit)) atomicMin(&first_invalid, static_cast<int>(k));
-    }
-    __syncthreads();
-    const int64_t first = first_invalid;
-    // 2. This block's share of the row: cleaned ids, malformed count.
-    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * p.blocks_per_cta;
-    const int64_t k1 = min(p.n_blocks, k0 + p.blocks_per_cta);
-    unsigned local[5] = {0, 0, 0, 0, 0};
-    for (int64_t k = k0 + threadIdx.x; k < k1; k += kShadowThreads) {
-        const int64_t block = load_index(p.blocks, p.blocks_es, b * p.blocks_row + k * p.blocks_col);
-        const bool valid = block >= 0 && block < limit;
-        const bool prefix = k < first;
-        local[4] += ((block != -1 && !valid) || (valid && !prefix)) ? 1u : 0u;
-        const int64_t c = prefix ? block : -1;
-        clean[k - k0] = c;
-        const int64_t at = b * p.n_blocks + k;
-        if (p.blocks_es == 8) {
-            static_cast<int64_t*>(p.clean_blocks)[at] = c;
-        } else {
-            static_cast<int32_t*>(p.clean_blocks)[at] = static_cast<int32_t>(c);
-        }
-    }
-    __syncthreads();
-    // 3. Tokens: one index chain per lane, then the warp compares the rows.
-    const int64_t tokens = (k1 - k0) * p.block_size;
-    const int64_t token0 = k0 * p.block_size;
     const int64_t width = p.n_blocks * p.block_size;
-    for (int64_t base = static_cast<int64_t>(warp) * 32; base < tokens; base += kShadowThreads) {
-        const int64_t t = base + lane;
+    const int64_t total = p.batch * width;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kShadowWarps;
+    const int64_t g = static_cast<int64_t>(blockIdx.x) * kShadowWarps + (threadIdx.x >> 5);
+    const int64_t begin = static_cast<int64_t>((static_cast<__int128>(total) * g) / warps);
+    const int64_t end = static_cast<int64_t>((static_cast<__int128>(total) * (g + 1)) / warps);
+    unsigned local[5] = {0, 0, 0, 0, 0};
+    for (int64_t base = begin; base < end; base += 32) {
+        const int64_t token = base + lane;
         bool checked = false;
         int64_t safe = 0, logical = 0;
-        if (t < tokens) {
+        if (token < end) {
+            const int64_t b = token / width;
+            const int64_t t = token - b * width;
             const int64_t kk = t / p.block_size;
             const int64_t j = t - kk * p.block_size;
-            const int64_t position = static_cast<int64_t>(static_cast<uint64_t>(clean[kk]) *
-                                                          static_cast<uint64_t>(p.block_size) + j);
+            const int64_t clean = load_index(p.clean_blocks, p.blocks_es, b * p.n_blocks + kk);
+            const int64_t length = load_index(p.lengths, p.len_es, b * p.len_stride);
+            const int64_t position =
+                static_cast<int64_t>(static_cast<uint64_t>(clean) * static_cast<uint64_t>(p.block_size) + j);
             const bool selected = position >= 0 && position < length;
             const bool bounded = selected && position < p.table_width;
             bool logical_valid = false;
             if (bounded) {
+                const int64_t req = load_index(p.rows, p.rows_es, b * p.rows_stride);
                 logical = load_index(p.table, p.table_es, req * p.table_row + position * p.table_col);
                 logical_valid = logical >= p.page_size && logical < p.capacity;
             }
             if (!logical_valid) logical = 0;
             const bool source_valid = logical_valid && p.initialized[logical] != 0;
-            const int64_t tg = token0 + t;
             const int64_t phys =
-                p.physical ? static_cast<int64_t>(p.physical[b * p.phys_row + tg * p.phys_col]) : logical;
+                p.physical ? static_cast<int64_t>(p.physical[b * p.phys_row + t * p.phys_col]) : logical;
             const bool in_range = phys >= p.page_size && phys < p.cache_rows;
             safe = in_range ? phys : 0;
             bool backed = in_range;
@@ -215,7 +231,7 @@ shadow_check_kernel(const __grid_constant__ CheckParams p) {
             local[0] += checked ? 1u : 0u;
             local[1] += (selected && !source_valid) ? 1u : 0u;
             local[2] += (selected && !backed) ? 1u : 0u;
-            p.physical_out[b * width + tg] = (selected && !backed) ? 0 : static_cast<int32_t>(phys);
+            p.physical_out[token] = (selected && !backed) ? 0 : static_cast<int32_t>(phys);
         }
         unsigned pending = __ballot_sync(0xffffffffu, checked);
         while (pending) {
@@ -230,7 +246,7 @@ shadow_check_kernel(const __grid_constant__ CheckParams p) {
             if (__any_sync(0xffffffffu, differ) && lane == static_cast<unsigned>(src)) local[3] += 1u;
         }
     }
-    add_counts(p.counts, local, block_sum, 5);
+    add_counts(p.counts, local, block_sum, 4);
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned long long checked = block_sum[0];
@@ -241,7 +257,6 @@ shadow_check_kernel(const __grid_constant__ CheckParams p) {
         if (block_sum[1]) atomicAdd(&p.counts[2], static_cast<unsigned long long>(block_sum[1]));
         if (block_sum[2]) atomicAdd(&p.counts[3], static_cast<unsigned long long>(block_sum[2]));
         if (block_sum[3]) atomicAdd(&p.counts[4], static_cast<unsigned long long>(block_sum[3]));
-        if (block_sum[4]) atomicAdd(&p.counts[6], static_cast<unsigned long long>(block_sum[4]));
     }
 }
 
@@ -479,19 +494,23 @@ extern "C" int ekv_shadow_check(
         p.len_es = len_esize;
         p.rows_es = rows_esize;
         p.table_es = table_esize;
-        const int64_t tile = tokens_per_block(batch * n_blocks * block_size, device);
-        p.blocks_per_cta = std::max<int64_t>(1, std::min<int64_t>(n_blocks, tile / block_size));
         p.vec = vector_width({reinterpret_cast<uint64_t>(k_cache), reinterpret_cast<uint64_t>(v_cache),
                               reinterpret_cast<uint64_t>(k_shadow), reinterpret_cast<uint64_t>(v_shadow),
                               static_cast<uint64_t>(k_cache_stride), static_cast<uint64_t>(v_cache_stride),
                               static_cast<uint64_t>(k_shadow_stride), static_cast<uint64_t>(v_shadow_stride),
                               static_cast<uint64_t>(k_row_bytes), static_cast<uint64_t>(v_row_bytes)});
-        const int64_t x = n_blocks > 0 ? (n_blocks + p.blocks_per_cta - 1) / p.blocks_per_cta : 1;
-        require(x <= 0x7fffffff, "grid too large");
-        const dim3 grid(static_cast<unsigned>(x), static_cast<unsigned>(std::max<int64_t>(1, p.batch)));
-        with_vector(p.vec, [&](auto v) {
-            shadow_check_kernel<decltype(v)><<<grid, kShadowThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-        });
+        const auto cstream = static_cast<cudaStream_t>(stream);
+        const int rows_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(p.batch, 65535)));
+        shadow_clean_kernel<<<rows_grid, kShadowThreads, 0, cstream>>>(p);
+        check_launch("shadow_clean launch");
+        const int64_t total = p.batch * n_blocks * block_size;
+        if (total > 0) {
+            const int64_t wanted = (total + kShadowThreads - 1) / kShadowThreads;
+            const int grid = static_cast<int>(std::min<int64_t>(wanted, static_cast<int64_t>(sm_count(device)) * 2));
+            with_vector(p.vec, [&](auto v) {
+                shadow_tokens_kernel<decltype(v)><<<grid, kShadowThreads, 0, cstream>>>(p);
+            });
+        }
         check_launch("shadow_check launch");
     });
 }
