@@ -72,6 +72,8 @@ def parse_args(argv=None):
     p.add_argument("--skip-migration", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
+    p.add_argument("--only", choices=("lookup", "shadow", "bitmap"), default=None,
+                   help="measurement aid: run one side leg alone (no config-2 pool) and print its JSON")
     p.add_argument("--tp-shard", type=int, default=0,
                    help="measurement aid: gather one rank's head shard of TP=N on this GPU "
                         "(default: the launch's world size)")
@@ -1320,8 +1322,12 @@ def main(argv=None):
         return 0
     dist = Dist()
     try:
-        runner = {4: run_config4, 5: run_config5}.get(args.config, run_ours)
-        result = runner(args, dist)
+        if args.only:
+            leg = {"lookup": lookup_bench, "shadow": shadow_bench, "bitmap": bitmap_bench}[args.only]
+            result = {"leg": args.only, **leg(dist)}
+        else:
+            runner = {4: run_config4, 5: run_config5}.get(args.config, run_ours)
+            result = runner(args, dist)
         if dist.rank == 0:
             print(json.dumps(result), file=out, flush=True)
     finally:

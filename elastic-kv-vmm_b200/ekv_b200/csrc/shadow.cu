@@ -505,7 +505,8 @@ extern "C" int ekv_shadow_check(
         check_launch("shadow_clean launch");
         const int64_t total = p.batch * n_blocks * block_size;
         if (total > 0) {
-            const int64_t wanted = (total + kShadowThreads - 1) / kShadowThreads;
+            // At least 16 tokens a warp, at most two resident blocks per SM.
+            const int64_t wanted = (total + kShadowWarps * 16 - 1) / (kShadowWarps * 16);
             const int grid = static_cast<int>(std::min<int64_t>(wanted, static_cast<int64_t>(sm_count(device)) * 2));
             with_vector(p.vec, [&](auto v) {
                 shadow_tokens_kernel<decltype(v)><<<grid, kShadowThreads, 0, cstream>>>(p);
