@@ -100,18 +100,23 @@ struct LookupParams {
     int map_es, topk_es, len_es;
 };
 
-constexpr int kLookupThreads = 512;
+constexpr int kLookupThreads = 256;
 constexpr int kLookupWarps = kLookupThreads / 32;
-constexpr int kLookupItems = 4;                             // consecutive columns per thread
-constexpr int kLookupTile = kLookupThreads * kLookupItems;  // columns per pass (2048)
 
-// One block per request row; a pass covers kLookupTile Top-K columns, each
-// thread kLookupItems consecutive ones, so a 2048-wide row is one pass with all
-// its independent map lookups in flight at once.  Misses are compacted in
-// column order by a block-wide exclusive scan of the per-thread miss counts
-// (warp shuffle scan, then a scan of the warp totals in shared memory).
+// One block per request row; a pass covers kLookupThreads * kItems Top-K
+// columns, each thread kItems consecutive ones, so a row of up to 2048 columns
+// is one pass with all its independent map lookups in flight at once (the
+// launch picks kItems = 2, 4 or 8, the smallest that covers the row).  Misses
+// are compacted in column order by a block-wide exclusive scan of the
+// per-thread miss counts (warp shuffle scan, then a scan of the warp totals in
+// shared memory).  256-thread blocks (at most 72 registers a thread) fit on an
+// SM beside two blocks of the gather kernel, so a layer's lookup can run while
+// the previous layer's gather does (swap.py's SwapPipeline).
+template <int kItems>
 __global__ void __launch_bounds__(kLookupThreads)
 lookup_kernel(const __grid_constant__ LookupParams p) {
+    constexpr int kLookupItems = kItems;
+    constexpr int kLookupTile = kLookupThreads * kItems;
     __shared__ int warp_totals[kLookupWarps];
     const unsigned lane = lane_id();
     const int warp = threadIdx.x >> 5;
@@ -290,7 +295,14 @@ extern "C" int ekv_lookup_slots(
         p.topk_es = topk_esize;
         p.len_es = lengths ? lengths_esize : 4;
         const unsigned grid = static_cast<unsigned>(batch < (1 << 20) ? batch : (1 << 20));
-        lookup_kernel<<<grid, kLookupThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        const auto cstream = static_cast<cudaStream_t>(stream);
+        if (k <= 2 * kLookupThreads) {
+            lookup_kernel<2><<<grid, kLookupThreads, 0, cstream>>>(p);
+        } else if (k <= 4 * kLookupThreads) {
+            lookup_kernel<4><<<grid, kLookupThreads, 0, cstream>>>(p);
+        } else {
+            lookup_kernel<8><<<grid, kLookupThreads, 0, cstream>>>(p);
+        }
         check_launch("lookup_slots launch");
     });
 }

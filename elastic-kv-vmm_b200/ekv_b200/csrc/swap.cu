@@ -145,8 +145,12 @@ struct PromoteParams {
     char* hot[EKV_MAX_PLANES];
 };
 
+#ifndef EKV_PROMOTE_BLOCKS_PER_SM
+#define EKV_PROMOTE_BLOCKS_PER_SM 1
+#endif
 constexpr int kPromoteThreads = 256;
 constexpr int kPromoteWarps = kPromoteThreads / 32;
+constexpr int kPromoteBlocksPerSm = EKV_PROMOTE_BLOCKS_PER_SM;
 
 template <typename T>
 __device__ __forceinline__ void warp_move(const char* src, char* dst, int64_t bytes, unsigned lane) {
@@ -168,29 +172,37 @@ __device__ __forceinline__ void warp_move(const char* src, char* dst, int64_t by
     }
 }
 
+// A fixed grid of EKV_PROMOTE_BLOCKS_PER_SM blocks per SM (8 warps each), one
+// 2 KiB row in flight per warp, leaves the SMs' other slots (registers: 2
+// gather blocks + 1 promote block fit) to a gather kernel running concurrently
+// on another stream.  Warps walk each request's miss list directly
+// (per_request warps share one request), so no time goes to the columns that
+// hit.
 __global__ void __launch_bounds__(kPromoteThreads)
 promote_kernel(const __grid_constant__ PromoteParams p) {
-    const int64_t tasks = p.batch * p.k * p.n_planes;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * kPromoteWarps;
+    const int64_t w = static_cast<int64_t>(blockIdx.x) * kPromoteWarps + (threadIdx.x >> 5);
     const unsigned lane = lane_id();
-    // Task order: plane fastest, so consecutive warps move one miss's K and V.
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kPromoteWarps + (threadIdx.x >> 5); t < tasks;
-         t += warps) {
-        const int64_t plane = t % p.n_planes;
-        const int64_t item = t / p.n_planes;
-        const int64_t b = item / p.k;
-        const int64_t r = item - b * p.k;
-        if (r >= p.miss_count[b]) continue;
-        const int32_t slot = p.promo_slot[b * p.promo_row + r];
-        const int32_t token = p.miss_list[b * p.list_row + r];
-        if (slot < 0 || token < 0 || token >= p.history_rows_per_request) continue;
-        const char* src = p.history[plane] + (b * p.history_rows_per_request + token) * p.row_bytes;
-        char* dst = p.hot[plane] + p.sink_bytes + b * p.request_bytes + static_cast<int64_t>(slot) * p.row_bytes;
-        const int64_t align = alignment_of(p.addr_or | static_cast<uint64_t>(p.row_bytes));
-        if (align == 16) {
-            warp_move<uint4>(src, dst, p.row_bytes, lane);
-        } else {
-            warp_move<uint8_t>(src, dst, p.row_bytes, lane);
+    const int64_t per_request = warps >= p.batch ? warps / p.batch : 1;
+    const int64_t request_stride = warps / per_request;
+    if (w >= per_request * request_stride) return;  // the remainder: every request is covered without it
+    const int64_t sub = w % per_request;
+    const int64_t align = alignment_of(p.addr_or | static_cast<uint64_t>(p.row_bytes));
+    for (int64_t b = w / per_request; b < p.batch; b += request_stride) {
+        const int64_t count = min(static_cast<int64_t>(p.miss_count[b]), p.k);
+        for (int64_t r = sub; r < count; r += per_request) {
+            const int32_t slot = p.promo_slot[b * p.promo_row + r];
+            const int32_t token = p.miss_list[b * p.list_row + r];
+            if (slot < 0 || token < 0 || token >= p.history_rows_per_request) continue;
+            const int64_t src_row = (b * p.history_rows_per_request + token) * p.row_bytes;
+            const int64_t dst_row = p.sink_bytes + b * p.request_bytes + static_cast<int64_t>(slot) * p.row_bytes;
+            for (int plane = 0; plane < p.n_planes; ++plane) {
+                if (align == 16) {
+                    warp_move<uint4>(p.history[plane] + src_row, p.hot[plane] + dst_row, p.row_bytes, lane);
+                } else {
+                    warp_move<uint8_t>(p.history[plane] + src_row, p.hot[plane] + dst_row, p.row_bytes, lane);
+                }
+            }
         }
     }
 }
@@ -284,12 +296,7 @@ extern "C" int ekv_promote_rows(
             addr_or |= reinterpret_cast<uint64_t>(view) | hot_planes[i];
         }
         p.addr_or = addr_or;
-        static int cached[64] = {0};
-        int grid = device < 64 ? cached[device] : 0;
-        if (!grid) {
-            grid = persistent_grid(reinterpret_cast<const void*>(promote_kernel), kPromoteThreads, 0, device);
-            if (device < 64) cached[device] = grid;
-        }
+        const int grid = sm_count(device) * kPromoteBlocksPerSm;
         promote_kernel<<<grid, kPromoteThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
         check_launch("promote_rows launch");
     });

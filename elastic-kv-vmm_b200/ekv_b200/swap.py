@@ -13,7 +13,8 @@ decode step is four launches, none of which waits for the host:
 4. mapped gather      Top-K rows read through the updated map.
 
 ``HotLayer`` holds one layer's state and runs the four steps; ``SwapStep`` is
-the pre-bound form for a hot loop or a CUDA graph.
+the pre-bound form for a hot loop or a CUDA graph; ``SwapPipeline`` runs a
+step's layers with each gather overlapped with the next layer's promotion.
 """
 
 from __future__ import annotations
@@ -144,9 +145,51 @@ class SwapStep:
         )
         self.device = dev
 
-    def __call__(self, stream: int | None = None) -> None:
+    def swap_in(self, stream: int | None = None) -> None:
+        """Steps 1-3: lookup, victim selection, promotion (host-link bound)."""
         stream = stream_handle(self.device) if stream is None else stream
         self.lookup(stream)
         call("ekv_swap_select", *self._select_args, stream)
         call("ekv_promote_rows", *self._promote_args, stream)
+
+    def __call__(self, stream: int | None = None) -> None:
+        stream = stream_handle(self.device) if stream is None else stream
+        self.swap_in(stream)
         self.gather(stream)
+
+
+class SwapPipeline:
+    """All layers of a decode step with each layer's gather overlapped with the next
+    layer's swap-in.
+
+    ``SwapStep`` runs its four launches in order, so the host-link-bound promotion
+    and the HBM-bound gather of a layer never overlap.  Here the lookups, victim
+    selections and promotions of all layers run in order on the caller's stream
+    and layer i's gather runs on a second stream as soon as layer i's promotion
+    is done (one event per layer), while layer i+1 promotes.  The promotion
+    kernel's small fixed grid leaves the SMs' other slots to the gather.  The
+    gathers stay in layer order on their stream, so layers may share one output
+    buffer; the caller's stream waits for the last gather before returning.
+    Works eagerly and under CUDA graph capture (the second stream forks from and
+    joins the caller's stream).
+    """
+
+    def __init__(self, plans):
+        self.plans = list(plans)
+        if not self.plans:
+            raise ValueError("need at least one layer")
+        self.device = self.plans[0].device
+        self.side = torch.cuda.Stream(self.device)
+        self.ready = [torch.cuda.Event() for _ in self.plans]
+
+    def __call__(self) -> None:
+        main = torch.cuda.current_stream(self.device)
+        side = self.side
+        side.wait_stream(main)  # fork: the gathers see everything issued before the step
+        main_handle, side_handle = main.cuda_stream, side.cuda_stream
+        for plan, ready in zip(self.plans, self.ready):
+            plan.swap_in(main_handle)
+            ready.record(main)
+            side.wait_event(ready)
+            plan.gather(side_handle)
+        main.wait_stream(side)  # join

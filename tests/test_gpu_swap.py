@@ -169,3 +169,77 @@ def test_multi_step_decode_matches_oracle(cuda_device):
                 # Size-independent property: every gathered row is the token's history row.
                 rows = np.arange(batch)[:, None] * context + topk
                 np.testing.assert_array_equal(got, hist_np[plane][rows])
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_pipeline_equals_layer_order(graph, cuda_device):
+    """SwapPipeline (layer i's gather on a second stream during layer i+1's promotion)
+    leaves exactly the state and outputs of running the layers in order, step after
+    step; with ``graph`` the pipelined step is captured once and replayed.  Layers share
+    one output pair, as a decode step does."""
+    from ekv_b200.host_pool import pinned_buffer
+    from ekv_b200.swap import HotLayer, SwapPipeline, SwapStep
+
+    rng = np.random.default_rng(21)
+    batch, context, hot, k, width, layers, steps = 16, 4096, 512, 256, 256, 6, 6
+    row_bytes = width * 2
+    histories = []
+    for _ in range(2):
+        h = pinned_buffer(batch * context * row_bytes)[: batch * context * row_bytes].view(batch * context, row_bytes)
+        h.copy_(torch.from_numpy(rng.integers(0, 256, (batch * context, row_bytes), dtype=np.uint8)))
+        histories.append(h)
+    hist_views = [h.view(torch.bfloat16) for h in histories]
+    dev = cuda_device
+    topk = np.stack([rng.choice(context, k, replace=False) for _ in range(batch)]).astype(np.int32)
+    topk_dev = torch.from_numpy(topk).to(dev)
+    runs = {}
+    for mode in ("ordered", "pipelined"):
+        topk_dev.copy_(torch.from_numpy(topk))  # each mode starts from the same step-0 Top-K
+        hot_layers = [HotLayer(batch, context, hot, width, dev, chunk_bytes=1 << 16) for _ in range(layers)]
+        shared = [torch.empty((batch, k, width), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        plans = [SwapStep(layer, topk_dev, hist_views, shared) for layer in hot_layers]
+        pipeline = SwapPipeline(plans)
+        replay = None
+        if graph and mode == "pipelined":
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                pipeline()  # warm-up outside capture: counts as step 0
+            torch.cuda.current_stream(dev).wait_stream(side)
+            torch.cuda.synchronize()
+            replay = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(replay):
+                pipeline()
+        local = np.random.default_rng(5)
+        ids = topk.copy()
+        outs, states = [], []
+        zipf = lambda r: context - 1 - min(int(r.zipf(1.1)) - 1, context - 1)  # noqa: E731
+        for step in range(steps):
+            if step:
+                ids = _evolve(local, ids, context, int(0.9 * k), zipf)
+            topk_dev.copy_(torch.from_numpy(ids))
+            if mode == "ordered":
+                if graph and step == 0:
+                    for plan in plans:
+                        plan()  # the pipelined run's warm-up step
+                for plan in plans:
+                    plan()
+            elif replay is not None:
+                replay.replay()
+            else:
+                pipeline()
+            torch.cuda.synchronize()
+            outs.append([o.view(torch.uint8).cpu().numpy().copy() for o in shared])
+            states.append([(l.res_map.cpu().numpy().copy(), l.slot_token.cpu().numpy().copy()) for l in hot_layers])
+            rows = np.arange(batch)[:, None] * context + ids
+            for plane in range(2):  # the last layer's rows are the tokens' history rows
+                np.testing.assert_array_equal(outs[-1][plane].reshape(batch, k, row_bytes),
+                                              histories[plane].numpy()[rows])
+        runs[mode] = (outs, states)
+        del replay
+    for step in range(steps):
+        for a, b in zip(runs["ordered"][0][step], runs["pipelined"][0][step]):
+            np.testing.assert_array_equal(a, b)
+        for (ma, ta), (mb, tb) in zip(runs["ordered"][1][step], runs["pipelined"][1][step]):
+            np.testing.assert_array_equal(ma, mb)
+            np.testing.assert_array_equal(ta, tb)
