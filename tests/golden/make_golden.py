@@ -26,10 +26,12 @@ from types import SimpleNamespace
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("EKV_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("EKV_REFERENCE", ""))
 
 
 def _import_reference():
+    if not os.environ.get("EKV_REFERENCE"):
+        raise SystemExit("set EKV_REFERENCE to the reference checkout")
     if os.environ.get("TRITON_INTERPRET") != "1":
         raise SystemExit("set TRITON_INTERPRET=1 so the reference Triton kernels run on CPU")
     sys.path.insert(0, str(REFERENCE))
@@ -316,6 +318,18 @@ def torch_module():
     return torch
 
 
+def _seed_shadow_layer(shadow, layer, key, value, gen):
+    """Create the layer with an empty write (the reference allocates it with
+    new_empty) and give its never-written rows seeded contents, so the fixture
+    does not depend on what the allocator returned."""
+    import torch
+
+    shadow.write(layer, torch.empty(0, dtype=torch.long), key[:0], value[:0], (None, None))
+    k, v, _ = shadow.layers[layer]
+    k.copy_(torch.randn(k.shape, generator=gen).to(k.dtype))
+    v.copy_(torch.randn(v.shape, generator=gen).to(v.dtype))
+
+
 def shadow_cases(ref):
     """LogicalShadow.check / check_complete (adaptive_sparse/logical_shadow.py:45-123).
 
@@ -343,6 +357,7 @@ def shadow_cases(ref):
         written = torch.randperm(capacity, generator=gen)[:120]
         key = torch.randn((120, heads, dim), generator=gen).to(torch.bfloat16)
         value = torch.randn((120, heads, dim), generator=gen).to(torch.bfloat16)
+        _seed_shadow_layer(shadow, 3, key, value, gen)
         shadow.write(3, written, key, value, (None, 1.0))
         k_shadow, v_shadow, initialized = shadow.layers[3]
         # The cache mirrors the shadow through a permutation; a few rows are corrupted.
@@ -404,6 +419,7 @@ def shadow_cases(ref):
             written = torch.randperm(capacity, generator=gen)[:80]
             key = torch.randn((80, heads, dim), generator=gen).to(torch.bfloat16)
             value = torch.randn((80, heads, dim), generator=gen).to(torch.bfloat16)
+            _seed_shadow_layer(shadow, 10 + layer, key, value, gen)
             shadow.write(10 + layer, written, key, value, (None, None))
             k, v, _ = shadow.layers[10 + layer]
             pk = torch.randn((size + page_size, heads, dim), generator=gen).to(torch.bfloat16)
