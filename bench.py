@@ -783,13 +783,13 @@ def shadow_complete_bench(shadow, dev, heads, dim, capacity, reps, layers=4, pai
 
 # --------------------------------------------------------------------------- bitmap (config 4 geometry)
 
-def bitmap_bench(dist: Dist, reps: int = 50):
+def bitmap_bench(dist: Dist, reps: int = 50, shard: int = 0):
     from ekv_b200.releasable import (ChunkProjection, bitmap_to_chunks, chunks_to_bitmap,
                                      combine_freeable, freeable_bitmap)
 
     dev = dist.device
     layers, n_chunks = 48, 4096
-    row_bytes = 2048 // dist.world
+    row_bytes = 2048 // (shard or dist.world)
     planes_n = 2 * layers
     per_plane = n_chunks // planes_n
     slots = per_plane * CHUNK // row_bytes
@@ -821,6 +821,27 @@ def bitmap_bench(dist: Dist, reps: int = 50):
     end.record(stream)
     torch.cuda.synchronize()
     build_ms = start.elapsed_time(end) / reps
+    # Device time of the build alone: `reps` builds into fixed buffers captured in
+    # one CUDA graph and replayed (the loop above is bound by host dispatch).
+    counts_buf = projection.counts(candidate)
+    bits_buf = freeable_bitmap(counts_buf, refs, mapped)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        freeable_bitmap(projection.counts(candidate, out=counts_buf), refs, mapped, out=bits_buf)
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            freeable_bitmap(projection.counts(candidate, out=counts_buf), refs, mapped, out=bits_buf)
+    graph.replay()
+    torch.cuda.synchronize()
+    start.record(stream)
+    graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    build_device_ms = start.elapsed_time(end) / reps
+    del graph
     dist.barrier()
     torch.cuda.synchronize()
     start.record(stream)
@@ -862,7 +883,8 @@ def bitmap_bench(dist: Dist, reps: int = 50):
     return {"chunks": n_chunks, "words": n_chunks // 64, "ranks": dist.world,
             "freeable_local": len(local_set), "freeable_joint": len(bitmap_to_chunks(joint)),
             "joint_matches_intersection": bitmap_to_chunks(joint) == expected_joint,
-            "build_us": build_ms * 1e3, "combine_us": combine_ms * 1e3,
+            "build_us": build_ms * 1e3, "build_device_us": build_device_ms * 1e3,
+            "pages": int(candidate.numel()), "planes": planes_n, "combine_us": combine_ms * 1e3,
             "combine": "NCCL all_gather_into_tensor + AND kernel" if dist.world > 1 else "single rank",
             **fused}
 
@@ -1349,8 +1371,11 @@ def main(argv=None):
     dist = Dist()
     try:
         if args.only:
-            leg = {"lookup": lookup_bench, "shadow": shadow_bench, "bitmap": bitmap_bench}[args.only]
-            result = {"leg": args.only, **leg(dist)}
+            if args.only == "bitmap":
+                leg_result = bitmap_bench(dist, shard=args.tp_shard)
+            else:
+                leg_result = {"lookup": lookup_bench, "shadow": shadow_bench}[args.only](dist)
+            result = {"leg": args.only, **leg_result}
         else:
             runner = {4: run_config4, 5: run_config5}.get(args.config, run_ours)
             result = runner(args, dist)

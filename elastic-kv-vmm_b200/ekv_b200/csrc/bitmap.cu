@@ -14,6 +14,8 @@
 // when the chunk table fits in shared memory each block accumulates a private
 // histogram there and flushes its non-zero bins once.  The bitmap is built with
 // warp ballots (32 chunks per ballot, two ballots per 64-bit word).
+#include <vector>
+
 #include "common.cuh"
 
 namespace ekv {
@@ -95,6 +97,86 @@ chunk_count_kernel(const __grid_constant__ CountParams p) {
         for (int64_t c = threadIdx.x; c < p.n_chunks; c += kCountThreads) {
             const int32_t v = shared_bins[c];
             if (v) atomicAdd(p.counts + c, v);
+        }
+    }
+}
+
+// Planes with the same row size map page g to the same chunk offsets relative
+// to their first chunk, so one histogram of relative chunk offsets over the
+// pages serves the whole group: block-private in shared memory (bin n_chunks
+// collects offsets past the table, which are past it for every plane), then
+// each non-zero bin is added to every plane of the group at that plane's first
+// chunk.  Work: n_pages histogram updates + (non-zero bins x planes) atomics,
+// instead of n_pages x planes.  Same counts and overflow as the per-plane
+// kernel; a negative page (offset < 0) takes the per-plane path inline.
+struct GroupParams {
+    const void* pages;
+    int32_t* counts;
+    int32_t* overflow;
+    int64_t n_pages, page_size, chunk_bytes, n_chunks, row_bytes;
+    int pages_es, n_planes;
+    int64_t plane_chunk[EKV_MAX_PLANES];
+};
+
+__global__ void __launch_bounds__(kCountThreads)
+grouped_count_kernel(const __grid_constant__ GroupParams p) {
+    extern __shared__ int32_t bins[];  // n_chunks + 1
+    for (int64_t c = threadIdx.x; c <= p.n_chunks; c += kCountThreads) bins[c] = 0;
+    __syncthreads();
+    const unsigned lane = lane_id();
+    const int64_t span = p.page_size * p.row_bytes;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kCountThreads;
+    const int64_t bound = (p.n_pages + 31) & ~int64_t{31};
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kCountThreads + threadIdx.x; t < bound; t += stride) {
+        int64_t first = 0, last = -1;
+        if (t < p.n_pages) {
+            const int64_t begin = load_index(p.pages, p.pages_es, t) * span;
+            // Truncating division, exactly as the per-plane kernel computes it.
+            first = begin / p.chunk_bytes;
+            last = (begin + span - 1) / p.chunk_bytes;
+        }
+        const int64_t steps = last - first + 1;
+        int64_t max_steps = steps;
+        for (int offset = 16; offset > 0; offset >>= 1) {
+            const int64_t other = __shfl_xor_sync(0xffffffffu, max_steps, offset);
+            max_steps = other > max_steps ? other : max_steps;
+        }
+        for (int64_t s = 0; s < max_steps; ++s) {
+            int64_t bin = -1;
+            if (s < steps) {
+                const int64_t rel = first + s;
+                if (rel < 0) {
+                    // Rare: a negative page.  Resolve it plane by plane, as the per-plane kernel does.
+                    for (int q = 0; q < p.n_planes; ++q) {
+                        const int64_t chunk = p.plane_chunk[q] + rel;
+                        if (chunk >= 0 && chunk < p.n_chunks) {
+                            atomicAdd(p.counts + chunk, 1);
+                        } else if (p.overflow) {
+                            atomicAdd(p.overflow, 1);
+                        }
+                    }
+                } else {
+                    bin = rel < p.n_chunks ? rel : p.n_chunks;
+                }
+            }
+            add_bin<true>(bins, bin, lane);
+        }
+    }
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c <= p.n_chunks; c += kCountThreads) {
+        const int32_t v = bins[c];
+        if (!v) continue;
+        if (c == p.n_chunks) {
+            if (p.overflow) atomicAdd(p.overflow, v * p.n_planes);
+            continue;
+        }
+        for (int q = 0; q < p.n_planes; ++q) {
+            const int64_t chunk = p.plane_chunk[q] + c;
+            if (chunk < p.n_chunks) {
+                atomicAdd(p.counts + chunk, v);
+            } else if (p.overflow) {
+                atomicAdd(p.overflow, v);
+            }
         }
     }
 }
@@ -186,7 +268,55 @@ extern "C" int ekv_chunk_counts(
             p.plane_chunk[i] = plane_chunk[i];
             p.plane_row_bytes[i] = plane_row_bytes[i];
         }
-        const int64_t tasks = n_pages * n_planes;
+        // Planes sharing a row size (usually all K and V planes) go through the
+        // grouped histogram when the chunk table fits in shared memory.
+        std::vector<char> grouped(n_planes, 0);
+        if (n_chunks < kSharedChunkLimit) {
+            static bool grouped_configured[64] = {false};
+            if (device < 64 && !grouped_configured[device]) {
+                cuda_check(cudaFuncSetAttribute(grouped_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                static_cast<int>(kSharedChunkLimit * sizeof(int32_t))),
+                           "configure grouped histogram");
+                grouped_configured[device] = true;
+            }
+            for (int i = 0; i < n_planes; ++i) {
+                if (grouped[i]) continue;
+                GroupParams g{};
+                g.pages = pages;
+                g.counts = counts;
+                g.overflow = overflow;
+                g.n_pages = n_pages;
+                g.page_size = page_size;
+                g.chunk_bytes = chunk_bytes;
+                g.n_chunks = n_chunks;
+                g.row_bytes = plane_row_bytes[i];
+                g.pages_es = pages_esize;
+                for (int j = i; j < n_planes; ++j) {
+                    if (plane_row_bytes[j] == plane_row_bytes[i]) g.plane_chunk[g.n_planes++] = plane_chunk[j];
+                }
+                if (g.n_planes < 2) continue;  // a lone plane: the per-plane kernel below
+                for (int j = i; j < n_planes; ++j) {
+                    if (plane_row_bytes[j] == plane_row_bytes[i]) grouped[j] = 1;
+                }
+                const int64_t needed = (n_pages + kCountThreads - 1) / kCountThreads;
+                const int64_t cap = sm_count(device);
+                const unsigned grid = static_cast<unsigned>(needed < cap ? needed : cap);
+                const size_t smem = static_cast<size_t>(n_chunks + 1) * sizeof(int32_t);
+                grouped_count_kernel<<<grid, kCountThreads, smem, s>>>(g);
+                check_launch("grouped chunk_counts launch");
+            }
+            int rest = 0;
+            for (int i = 0; i < n_planes; ++i) {
+                if (!grouped[i]) {
+                    p.plane_chunk[rest] = plane_chunk[i];
+                    p.plane_row_bytes[rest] = plane_row_bytes[i];
+                    ++rest;
+                }
+            }
+            if (!rest) return;
+            p.n_planes = rest;
+        }
+        const int64_t tasks = n_pages * p.n_planes;
         if (n_chunks <= kSharedChunkLimit) {
             const size_t smem = static_cast<size_t>(n_chunks) * sizeof(int32_t);
             static bool configured[64] = {false};

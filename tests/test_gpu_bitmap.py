@@ -193,3 +193,39 @@ def test_peer_combine_wait_gives_up_with_a_status(cuda_device):
     alone = PeerFreeableCombiner(n, cuda_device, buffers=[mine.data_ptr()], rank=0, max_polls=10)
     assert torch.equal(alone.combine(local_bits=bits), bits)
     assert not alone.failed()
+
+
+def _overflow_np(pages, planes, page_size, chunk_bytes, n_chunks):
+    """(page, plane, chunk) hits outside [0, n_chunks) for non-negative pages."""
+    total = 0
+    pages = np.asarray(pages, dtype=np.int64)
+    for first_chunk, row_bytes in planes:
+        span = page_size * row_bytes
+        lo = first_chunk + pages * span // chunk_bytes
+        hi = first_chunk + (pages * span + span - 1) // chunk_bytes
+        for page_lo, page_hi in zip(lo, hi):
+            c = np.arange(page_lo, page_hi + 1)
+            total += int(((c < 0) | (c >= n_chunks)).sum())
+    return total
+
+
+@pytest.mark.parametrize("n_chunks", [700, 70_000])
+def test_counts_with_plane_groups_straddles_and_overflow(n_chunks, cuda_device):
+    """Planes sharing a row size go through one grouped histogram (shared-memory tables),
+    lone planes through the per-plane kernel; pages that straddle chunk boundaries and
+    chunks past the table (counted in ``overflow``) give the same answers either way."""
+    from ekv_b200.releasable import ChunkProjection
+
+    gen = torch.Generator().manual_seed(n_chunks)
+    chunk_bytes, page_size = 512, 3
+    rows = [96] * 6 + [40, 40] + [1000]  # a group of 6, a group of 2, a lone plane
+    planes = [(i * (n_chunks // 12), r) for i, r in enumerate(rows)]
+    pages = torch.randperm(4000, generator=gen)[:1500] + 1
+    projection = ChunkProjection(planes, page_size, chunk_bytes, n_chunks, cuda_device)
+    got = projection.counts(pages.to(cuda_device))
+    want = orl.chunk_counts_np(pages.numpy(), planes, page_size, chunk_bytes, n_chunks)
+    np.testing.assert_array_equal(got.cpu().numpy(), want)
+    want_overflow = _overflow_np(pages.numpy(), planes, page_size, chunk_bytes, n_chunks)
+    assert int(projection.overflow.item()) == want_overflow
+    if n_chunks == 700:
+        assert want_overflow > 0  # the last planes run past the table
