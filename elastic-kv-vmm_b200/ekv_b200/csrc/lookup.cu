@@ -100,20 +100,28 @@ struct LookupParams {
     int map_es, topk_es, len_es;
 };
 
-constexpr int kLookupThreads = 256;
+#ifndef EKV_LOOKUP_THREADS
+#define EKV_LOOKUP_THREADS 512
+#endif
+#ifndef EKV_LOOKUP_MIN_BLOCKS
+#define EKV_LOOKUP_MIN_BLOCKS 3
+#endif
+constexpr int kLookupThreads = EKV_LOOKUP_THREADS;
 constexpr int kLookupWarps = kLookupThreads / 32;
 
 // One block per request row; a pass covers kLookupThreads * kItems Top-K
 // columns, each thread kItems consecutive ones, so a row of up to 2048 columns
 // is one pass with all its independent map lookups in flight at once (the
-// launch picks kItems = 2, 4 or 8, the smallest that covers the row).  Misses
-// are compacted in column order by a block-wide exclusive scan of the
-// per-thread miss counts (warp shuffle scan, then a scan of the warp totals in
-// shared memory).  256-thread blocks (at most 72 registers a thread) fit on an
-// SM beside two blocks of the gather kernel, so a layer's lookup can run while
-// the previous layer's gather does (swap.py's SwapPipeline).
+// launch picks kItems = 1, 2 or 4; wider rows take several passes).  Misses are
+// compacted in column order by a block-wide exclusive scan of the per-thread
+// miss counts (warp shuffle scan, then a scan of the warp totals in shared
+// memory).  The register cap of 3 blocks per SM (40 registers a thread, no
+// spills) lets a 512-thread block fit on an SM beside two blocks of the gather
+// kernel, so a layer's lookup can run while the previous layer's gather does
+// (swap.py's SwapPipeline); 16 warps per row hide the two dependent loads
+// better than 8 (256-thread blocks measured 6 % slower on config 4).
 template <int kItems>
-__global__ void __launch_bounds__(kLookupThreads)
+__global__ void __launch_bounds__(kLookupThreads, EKV_LOOKUP_MIN_BLOCKS)
 lookup_kernel(const __grid_constant__ LookupParams p) {
     constexpr int kLookupItems = kItems;
     constexpr int kLookupTile = kLookupThreads * kItems;
@@ -296,12 +304,12 @@ extern "C" int ekv_lookup_slots(
         p.len_es = lengths ? lengths_esize : 4;
         const unsigned grid = static_cast<unsigned>(batch < (1 << 20) ? batch : (1 << 20));
         const auto cstream = static_cast<cudaStream_t>(stream);
-        if (k <= 2 * kLookupThreads) {
+        if (k <= kLookupThreads) {
+            lookup_kernel<1><<<grid, kLookupThreads, 0, cstream>>>(p);
+        } else if (k <= 2 * kLookupThreads) {
             lookup_kernel<2><<<grid, kLookupThreads, 0, cstream>>>(p);
-        } else if (k <= 4 * kLookupThreads) {
-            lookup_kernel<4><<<grid, kLookupThreads, 0, cstream>>>(p);
         } else {
-            lookup_kernel<8><<<grid, kLookupThreads, 0, cstream>>>(p);
+            lookup_kernel<4><<<grid, kLookupThreads, 0, cstream>>>(p);
         }
         check_launch("lookup_slots launch");
     });
