@@ -209,6 +209,39 @@ def library(path: str | None = None) -> ct.CDLL:
     return lib
 
 
+TORCH_BINDING_PATH = LIBRARY_PATH.parent / "_ekv_torch.so"
+
+
+@functools.lru_cache(maxsize=None)
+def torch_binding():
+    """The compiled pybind11 binding of the per-call lookups, or None.
+
+    It calls the same C entry points of the library loaded above (their
+    addresses are handed over here), reading tensor pointers and strides in C++
+    instead of Python; a call it does not handle (unusual arguments) reports so
+    and the ctypes path runs.  EKV_B200_NO_TORCH_BINDING=1 disables it.
+    """
+    if os.environ.get("EKV_B200_NO_TORCH_BINDING") or not TORCH_BINDING_PATH.exists():
+        return None
+    import importlib.util
+
+    try:
+        spec = importlib.util.spec_from_file_location("_ekv_torch", TORCH_BINDING_PATH)
+        module = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(module)
+    except (ImportError, OSError):
+        return None
+    lib = library()
+    module.bind(ct.cast(lib.ekv_resolve_resident, ct.c_void_p).value,
+                ct.cast(lib.ekv_lookup_slots, ct.c_void_p).value)
+    return module
+
+
+def last_error(name: str) -> KernelError:
+    """KernelError carrying the library's message for the last failed call of this thread."""
+    return KernelError(f"{name}: {library().ekv_error().decode('utf-8', 'replace')}")
+
+
 def call(name: str, *args) -> None:
     """Invoke a kernel entry point; raise KernelError with its message on failure."""
     lib = library()

@@ -93,6 +93,32 @@ def build(verbose: bool = False, force: bool = False, ptxas_info: bool = False) 
     return LIBRARY
 
 
+TORCH_BINDING = PACKAGE / "lib" / "_ekv_torch.so"
+
+
+def build_torch_binding(verbose: bool = False, force: bool = False) -> Path | None:
+    """Compile the optional pybind11 binding of the per-call lookups (csrc/torch_binding.cpp)
+    against this interpreter's torch; return its path, or None (with a warning) when it
+    cannot be built -- the ctypes binding then serves every call."""
+    source = CSRC / "torch_binding.cpp"
+    if not force and not _stale(TORCH_BINDING, [source, *INCLUDE.glob("*.h")]):
+        return TORCH_BINDING
+    try:
+        from torch.utils.cpp_extension import load
+
+        out = BUILD_DIR / "torch_binding"
+        out.mkdir(parents=True, exist_ok=True)
+        load(name="_ekv_torch", sources=[str(source)], extra_include_paths=[str(INCLUDE)],
+             build_directory=str(out), with_cuda=True, verbose=verbose)
+        built = out / "_ekv_torch.so"
+        shutil.copy2(built, TORCH_BINDING.with_suffix(".so.tmp"))
+        os.replace(TORCH_BINDING.with_suffix(".so.tmp"), TORCH_BINDING)
+        return TORCH_BINDING
+    except Exception as exc:  # the binding is an accelerator of the host glue, not a compute path
+        print(f"warning: torch binding not built ({type(exc).__name__}: {exc})", file=sys.stderr)
+        return None
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--verbose", action="store_true")
@@ -100,6 +126,7 @@ def main(argv=None) -> int:
     parser.add_argument("--ptxas-info", action="store_true", help="print registers/spills per kernel")
     args = parser.parse_args(argv)
     path = build(verbose=args.verbose, force=args.force, ptxas_info=args.ptxas_info)
+    build_torch_binding(verbose=args.verbose, force=args.force)
     print(path)
     return 0
 

@@ -1,0 +1,147 @@
+// Compiled Python binding of the per-call residency lookups (optional).
+//
+// resolve_resident and lookup_slots are called once per layer per decode step
+// through the reference's Python API.  Through ctypes a call costs ~10 us of
+// host time (reading ~30 tensor attributes in Python and marshalling ~28
+// arguments); here the tensors arrive as at::Tensor and their pointers,
+// strides and the current stream are read in C++.  The kernels are reached
+// through the SAME C entry points of libekv_b200.so: Python hands over their
+// addresses once (bind), so this module does not link against the library.
+//
+// Only the well-formed calls are handled here: every tensor on one CUDA
+// device, supported dtypes and shapes.  Anything else returns kNotHandled and
+// the Python wrapper runs its checked ctypes path, which raises the documented
+// errors -- so error types and messages stay exactly those of the Python API.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <cstdint>
+#include <optional>
+
+#include "ekv_kernels.h"
+
+namespace {
+
+constexpr int kNotHandled = 1;  // ask the caller to take its checked path
+constexpr int kKernelError = -1;
+
+decltype(&ekv_resolve_resident) g_resolve = nullptr;
+decltype(&ekv_lookup_slots) g_lookup = nullptr;
+
+void bind(int64_t resolve, int64_t lookup) {
+    g_resolve = reinterpret_cast<decltype(&ekv_resolve_resident)>(resolve);
+    g_lookup = reinterpret_cast<decltype(&ekv_lookup_slots)>(lookup);
+}
+
+int index_size(const at::Tensor& t) {
+    switch (t.scalar_type()) {
+        case at::kInt: return 4;
+        case at::kLong: return 8;
+        default: return 0;
+    }
+}
+
+// All defined tensors CUDA on one device; the device index, or -1.
+int common_device(std::initializer_list<const at::Tensor*> tensors) {
+    int device = -1;
+    for (const at::Tensor* t : tensors) {
+        if (!t || !t->defined()) continue;
+        if (!t->is_cuda()) return -1;
+        const int here = t->get_device();
+        if (device < 0) {
+            device = here;
+        } else if (here != device) {
+            return -1;
+        }
+    }
+    return device;
+}
+
+void* stream_of(int device) { return c10::cuda::getCurrentCUDAStream(device).stream(); }
+
+int resolve_resident(const at::Tensor& topk, const at::Tensor& table, const at::Tensor& mapping,
+                     const at::Tensor& rows, const at::Tensor& lengths, const at::Tensor& selected,
+                     const at::Tensor& output, int64_t block_size) {
+    if (!g_resolve || topk.dim() != 3) return kNotHandled;
+    const int64_t width = topk.size(2) * block_size;
+    if (selected.numel() == 0 || width == 0) return 0;  // no-op, as the reference
+    const int device = common_device({&topk, &table, &mapping, &rows, &lengths, &selected, &output});
+    if (device < 0 || output.scalar_type() != at::kInt || table.dim() != 2 || output.dim() != 3) return kNotHandled;
+    const int es_topk = index_size(topk), es_table = index_size(table), es_map = index_size(mapping);
+    const int es_rows = index_size(rows), es_len = index_size(lengths), es_sel = index_size(selected);
+    if (!es_topk || !es_table || !es_map || !es_rows || !es_len || !es_sel) return kNotHandled;
+    const int rc = g_resolve(
+        topk.data_ptr(), es_topk, topk.stride(1), topk.stride(2), topk.size(2),
+        table.data_ptr(), es_table, table.stride(0), table.stride(1),
+        mapping.data_ptr(), es_map, mapping.stride(0),
+        rows.data_ptr(), es_rows, rows.stride(0),
+        lengths.data_ptr(), es_len, lengths.stride(0),
+        selected.data_ptr(), es_sel, selected.stride(0), selected.numel(),
+        output.data_ptr<int32_t>(), output.stride(1), output.stride(2),
+        block_size, device, stream_of(device));
+    return rc == 0 ? 0 : kKernelError;
+}
+
+bool rows_of(const std::optional<at::Tensor>& t, int device, at::ScalarType dtype, int64_t batch) {
+    if (!t) return true;
+    return t->is_cuda() && t->get_device() == device && t->scalar_type() == dtype && t->dim() >= 1 &&
+           t->size(0) == batch && t->stride(-1) == 1;
+}
+
+// Returns (status, slots, miss, miss_list, miss_count); outputs not given are allocated.
+py::tuple lookup_slots(const at::Tensor& residency_map, const at::Tensor& topk,
+                       const std::optional<at::Tensor>& lengths, std::optional<at::Tensor> slots,
+                       std::optional<at::Tensor> miss, std::optional<at::Tensor> miss_list,
+                       std::optional<at::Tensor> miss_count, bool compact) {
+    auto not_handled = [] { return py::make_tuple(kNotHandled, py::none(), py::none(), py::none(), py::none()); };
+    if (!g_lookup || residency_map.dim() != 2 || topk.dim() != 2 || residency_map.size(0) != topk.size(0)) {
+        return not_handled();
+    }
+    const at::Tensor* len_ptr = lengths ? &*lengths : nullptr;
+    const int device = common_device({&residency_map, &topk, len_ptr});
+    if (device < 0 || residency_map.stride(1) != 1 || topk.stride(1) != 1) return not_handled();
+    const int es_map = index_size(residency_map), es_topk = index_size(topk);
+    const int es_len = lengths ? index_size(*lengths) : 4;
+    if (!es_map || !es_topk || !es_len) return not_handled();
+    const int64_t batch = topk.size(0), k = topk.size(1);
+    if (lengths && (lengths->dim() != 1 || lengths->size(0) != batch || lengths->stride(0) != 1)) {
+        return not_handled();
+    }
+    const auto options = residency_map.options();
+    if (!slots) slots = at::empty({batch, k}, options.dtype(at::kInt));
+    if (!miss) miss = at::empty({batch, k}, options.dtype(at::kBool));
+    if (compact) {
+        if (!miss_list) miss_list = at::empty({batch, k}, options.dtype(at::kInt));
+        if (!miss_count) miss_count = at::empty({batch}, options.dtype(at::kInt));
+    }
+    if (!rows_of(slots, device, at::kInt, batch) || !rows_of(miss, device, at::kBool, batch) ||
+        !rows_of(miss_list, device, at::kInt, batch) || !rows_of(miss_count, device, at::kInt, batch) ||
+        (miss_count && miss_count->numel() != batch)) {
+        return not_handled();
+    }
+    const int rc = g_lookup(
+        residency_map.data_ptr(), es_map, residency_map.stride(0), residency_map.size(1),
+        topk.data_ptr(), es_topk, topk.stride(0),
+        lengths ? lengths->data_ptr() : nullptr, es_len,
+        batch, k,
+        slots->data_ptr<int32_t>(), slots->stride(0),
+        reinterpret_cast<uint8_t*>(miss->data_ptr()), miss->stride(0),
+        miss_list ? miss_list->data_ptr<int32_t>() : nullptr, miss_list ? miss_list->stride(0) : 0,
+        miss_count ? miss_count->data_ptr<int32_t>() : nullptr,
+        device, stream_of(device));
+    auto opt = [](const std::optional<at::Tensor>& t) { return t ? py::cast(*t) : py::none(); };
+    return py::make_tuple(rc == 0 ? 0 : kKernelError, py::cast(*slots), py::cast(*miss), opt(miss_list),
+                          opt(miss_count));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.doc() = "Compiled binding of the per-call residency lookups of libekv_b200.so";
+    m.def("bind", &bind, "set the addresses of the C entry points");
+    m.def("resolve_resident", &resolve_resident);
+    m.def("lookup_slots", &lookup_slots, py::arg("residency_map"), py::arg("topk"), py::arg("lengths"),
+          py::arg("slots"), py::arg("miss"), py::arg("miss_list"), py::arg("miss_count"), py::arg("compact"));
+    m.attr("NOT_HANDLED") = kNotHandled;
+    m.attr("KERNEL_ERROR") = kKernelError;
+}

@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import call, index_esize, require_cuda, stream_handle
+from ._lib import call, index_esize, last_error, require_cuda, stream_handle, torch_binding
 
 
 def resolve_resident(topk, table, mapping, rows, lengths, selected, output, block_size):
@@ -30,6 +30,16 @@ def resolve_resident(topk, table, mapping, rows, lengths, selected, output, bloc
     is truncated on store, as in the reference).  No-op when ``selected`` is
     empty or the width is zero (resident_lookup.py:31-33).
     """
+    fast = torch_binding()
+    if fast is not None and type(block_size) is int:
+        try:
+            rc = fast.resolve_resident(topk, table, mapping, rows, lengths, selected, output, block_size)
+        except TypeError:  # not tensors: the checked path below reports it
+            rc = fast.NOT_HANDLED
+        if rc == 0:
+            return
+        if rc == fast.KERNEL_ERROR:
+            raise last_error("ekv_resolve_resident")
     width = topk.shape[2] * block_size
     if not selected.numel() or not width:
         return
@@ -103,6 +113,17 @@ def lookup_slots(residency_map, topk, lengths=None, *, slots=None, miss=None, mi
     allocation.  With ``compact=False`` only ``slots`` and ``miss`` are
     produced.
     """
+    fast = torch_binding()
+    if fast is not None:
+        try:
+            rc, *results = fast.lookup_slots(residency_map, topk, lengths, slots, miss, miss_list, miss_count,
+                                             bool(compact))
+        except TypeError:  # not tensors: the checked path below reports it
+            rc = fast.NOT_HANDLED
+        if rc == 0:
+            return tuple(results)
+        if rc == fast.KERNEL_ERROR:
+            raise last_error("ekv_lookup_slots")
     device = require_cuda(dict(residency_map=residency_map, topk=topk, lengths=lengths))
     if residency_map.dim() != 2 or topk.dim() != 2 or residency_map.shape[0] != topk.shape[0]:
         raise ValueError("expected residency_map [B, T] and topk [B, K]")

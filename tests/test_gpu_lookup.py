@@ -139,3 +139,36 @@ def test_resolve_resident_config_scale_matches_torch_resolver(cuda_device):
     np.testing.assert_array_equal(got[0, selected.numpy()], expected)
     untouched = np.setdiff1d(np.arange(batch), selected.numpy())
     assert (got[0, untouched] == -77).all()
+
+
+def test_compiled_binding_is_loaded_and_matches_the_ctypes_path(cuda_device, monkeypatch):
+    """The pybind11 binding serves resolve_resident / lookup_slots when it is built, and
+    gives the same results as the ctypes path (forced by hiding the binding)."""
+    from ekv_b200 import _lib, resident_lookup
+
+    assert _lib.torch_binding() is not None, "lib/_ekv_torch.so was not built"
+    gen = torch.Generator().manual_seed(31)
+    batch, ctx, k = 8, 4096, 300
+    res_map = torch.full((batch, ctx), -1, dtype=torch.int32)
+    for b in range(batch):
+        tokens = torch.randperm(ctx, generator=gen)[:1000]
+        res_map[b, tokens] = torch.randperm(1000, generator=gen).to(torch.int32)
+    topk = torch.randint(-5, ctx + 5, (batch, k), generator=gen, dtype=torch.int32)
+    lengths = torch.randint(ctx // 2, ctx + 1, (batch,), generator=gen, dtype=torch.int64)
+    args = (res_map.to(cuda_device), topk.to(cuda_device), lengths.to(cuda_device))
+    fast = [t.cpu() for t in resident_lookup.lookup_slots(*args)]
+    table = torch.randint(0, 5000, (6, 512), generator=gen, dtype=torch.int64)
+    mapping = torch.randint(-2, 1 << 20, (5001,), generator=gen, dtype=torch.int64)
+    blocks = torch.randint(-1, 40, (1, 6, 16), generator=gen, dtype=torch.int32)
+    rows, lens, sel = torch.tensor([5, 4, 3, 2, 1, 0]), torch.randint(1, 512, (6,), generator=gen), torch.tensor([0, 2, 5])
+    res_args = [t.to(cuda_device) for t in (blocks, table, mapping, rows, lens, sel)]
+    out_fast = torch.full((1, 6, 16 * 8), -77, dtype=torch.int32, device=cuda_device)
+    resident_lookup.resolve_resident(*res_args, out_fast, 8)
+    monkeypatch.setattr(resident_lookup, "torch_binding", lambda: None)
+    slow = [t.cpu() for t in resident_lookup.lookup_slots(*args)]
+    out_slow = torch.full((1, 6, 16 * 8), -77, dtype=torch.int32, device=cuda_device)
+    resident_lookup.resolve_resident(*res_args, out_slow, 8)
+    for a, b in zip(fast, slow):
+        assert torch.equal(a, b)
+    assert torch.equal(out_fast, out_slow)
+    assert (out_fast[0, 1] == -77).all()  # rows not selected stay untouched
