@@ -233,7 +233,8 @@ def torch_binding():
         return None
     lib = library()
     module.bind(ct.cast(lib.ekv_resolve_resident, ct.c_void_p).value,
-                ct.cast(lib.ekv_lookup_slots, ct.c_void_p).value)
+                ct.cast(lib.ekv_lookup_slots, ct.c_void_p).value,
+                ct.cast(lib.ekv_resolve_shared_blocks, ct.c_void_p).value)
     return module
 
 

@@ -1,6 +1,7 @@
 // Compiled Python binding of the per-call residency lookups (optional).
 //
-// resolve_resident and lookup_slots are called once per layer per decode step
+// resolve_resident, lookup_slots and the batched shared-prefix resolver are
+// called once per layer per decode step
 // through the reference's Python API.  Through ctypes a call costs ~10 us of
 // host time (reading ~30 tensor attributes in Python and marshalling ~28
 // arguments); here the tensors arrive as at::Tensor and their pointers,
@@ -16,7 +17,9 @@
 #include <c10/cuda/CUDAStream.h>
 
 #include <cstdint>
+#include <limits>
 #include <optional>
+#include <vector>
 
 #include "ekv_kernels.h"
 
@@ -27,10 +30,12 @@ constexpr int kKernelError = -1;
 
 decltype(&ekv_resolve_resident) g_resolve = nullptr;
 decltype(&ekv_lookup_slots) g_lookup = nullptr;
+decltype(&ekv_resolve_shared_blocks) g_shared = nullptr;
 
-void bind(int64_t resolve, int64_t lookup) {
+void bind(int64_t resolve, int64_t lookup, int64_t shared) {
     g_resolve = reinterpret_cast<decltype(&ekv_resolve_resident)>(resolve);
     g_lookup = reinterpret_cast<decltype(&ekv_lookup_slots)>(lookup);
+    g_shared = reinterpret_cast<decltype(&ekv_resolve_shared_blocks)>(shared);
 }
 
 int index_size(const at::Tensor& t) {
@@ -134,6 +139,72 @@ py::tuple lookup_slots(const at::Tensor& residency_map, const at::Tensor& topk,
                           opt(miss_count));
 }
 
+// Exact Python ints only (bool and int subclasses take the checked path); false
+// when an element is not one, overflows int64 or falls outside [lo, hi).
+bool int_list(const py::sequence& seq, int64_t lo, int64_t hi, std::vector<int64_t>& out) {
+    const size_t n = py::len(seq);
+    out.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+        PyObject* item = PySequence_GetItem(seq.ptr(), static_cast<Py_ssize_t>(i));
+        if (!item) {
+            PyErr_Clear();
+            return false;
+        }
+        const bool exact = PyLong_CheckExact(item);
+        int overflow = 0;
+        const long long value = exact ? PyLong_AsLongLongAndOverflow(item, &overflow) : 0;
+        Py_DECREF(item);
+        if (!exact || overflow || value < lo || value >= hi) {
+            PyErr_Clear();
+            return false;
+        }
+        out[i] = value;
+    }
+    return true;
+}
+
+// resolve_shared_block_locations_batched: (status, valid, physical).
+py::tuple shared_blocks(const at::Tensor& block_ids, const py::sequence& source_rows, const at::Tensor& seq_len,
+                        const py::sequence& shared_tokens, int64_t block_size, const at::Tensor& table,
+                        const at::Tensor& mapping, bool exclude_newest, std::optional<at::Tensor> masked) {
+    auto not_handled = [] { return py::make_tuple(kNotHandled, py::none(), py::none()); };
+    if (!g_shared || block_ids.dim() != 2 || block_size < 1 || block_size > (int64_t{1} << 30) ||
+        table.dim() != 2 || table.size(1) == 0 || mapping.dim() != 1 || mapping.numel() == 0 ||
+        seq_len.dim() != 1) {
+        return not_handled();
+    }
+    const int64_t requests = block_ids.size(0), per_request = block_ids.size(1);
+    const at::Tensor* masked_ptr = masked ? &*masked : nullptr;
+    const int device = common_device({&block_ids, &seq_len, &table, &mapping, masked_ptr});
+    const int es_blocks = index_size(block_ids), es_len = index_size(seq_len);
+    const int es_table = index_size(table), es_map = index_size(mapping);
+    if (device < 0 || requests == 0 || per_request == 0 || requests > EKV_SHARED_INLINE_MAX || !es_blocks ||
+        !es_len || !es_table || !es_map || seq_len.numel() != requests) {
+        return not_handled();
+    }
+    if (masked && (masked->sizes() != block_ids.sizes() || masked->scalar_type() != block_ids.scalar_type() ||
+                   masked->strides() != block_ids.strides())) {
+        return not_handled();
+    }
+    std::vector<int64_t> rows, prefixes;
+    if (!int_list(source_rows, 0, table.size(0), rows) ||
+        !int_list(shared_tokens, 0, std::numeric_limits<int64_t>::max(), prefixes) ||
+        static_cast<int64_t>(rows.size()) != requests || static_cast<int64_t>(prefixes.size()) != requests) {
+        return not_handled();
+    }
+    const auto options = block_ids.options();
+    at::Tensor valid = at::empty({requests, per_request}, options.dtype(at::kBool));
+    at::Tensor physical = at::empty({requests, per_request, block_size}, options.dtype(at::kInt));
+    const int rc = g_shared(
+        block_ids.data_ptr(), es_blocks, requests, per_request, block_ids.stride(0), block_ids.stride(1),
+        rows.data(), 0, prefixes.data(), 0, seq_len.data_ptr(), es_len, seq_len.stride(0), block_size,
+        table.data_ptr(), es_table, table.size(0), table.size(1), table.stride(0), table.stride(1),
+        mapping.data_ptr(), es_map, mapping.numel(), mapping.stride(0), 1,
+        reinterpret_cast<uint8_t*>(valid.data_ptr()), physical.data_ptr<int32_t>(),
+        masked ? masked->data_ptr() : nullptr, exclude_newest ? 1 : 0, device, stream_of(device));
+    return py::make_tuple(rc == 0 ? 0 : kKernelError, valid, physical);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -142,6 +213,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("resolve_resident", &resolve_resident);
     m.def("lookup_slots", &lookup_slots, py::arg("residency_map"), py::arg("topk"), py::arg("lengths"),
           py::arg("slots"), py::arg("miss"), py::arg("miss_list"), py::arg("miss_count"), py::arg("compact"));
+    m.def("shared_blocks", &shared_blocks);
     m.attr("NOT_HANDLED") = kNotHandled;
     m.attr("KERNEL_ERROR") = kKernelError;
 }

@@ -20,7 +20,7 @@ import torch
 
 import numpy as np
 
-from ._lib import SHARED_INLINE_MAX, call, index_esize, stream_handle
+from ._lib import SHARED_INLINE_MAX, call, index_esize, last_error, stream_handle, torch_binding
 
 
 def _is_int(value) -> bool:
@@ -152,6 +152,18 @@ def resolve_shared_block_locations_batched(
     ``block_ids`` itself) receives the block ids with valid blocks set to -1
     (request_residency.py:231).
     """
+    fast = torch_binding()
+    if fast is not None and type(block_size) is int:
+        try:
+            rc, valid, physical = fast.shared_blocks(block_ids, source_rows, seq_len, shared_tokens, block_size,
+                                                     request_table, device_mapping, bool(exclude_newest),
+                                                     masked_block_ids)
+        except TypeError:  # not tensors / not sequences: the checked path below reports it
+            rc = fast.NOT_HANDLED
+        if rc == 0:
+            return valid, physical
+        if rc == fast.KERNEL_ERROR:
+            raise last_error("ekv_resolve_shared_blocks")
     if block_ids.ndim != 2:
         raise ValueError("block ids must be two-dimensional")
     request_count, blocks_per_request = block_ids.shape

@@ -153,3 +153,30 @@ def test_metadata_in_launch_parameters_and_on_the_device(requests, cuda_device):
         block_size=2, request_table=table.to(cuda_device), device_mapping=mapping.to(cuda_device))
     np.testing.assert_array_equal(valid.cpu().numpy(), want_valid)
     np.testing.assert_array_equal(physical.cpu().numpy(), want_physical)
+
+
+def test_compiled_binding_matches_the_ctypes_path(cuda_device, monkeypatch):
+    """The pybind11 binding serves the batched resolver (lists checked in C++) and gives
+    the results of the ctypes path; lists it does not take (bools, numpy ints) go to the
+    checked path, which answers as the reference does."""
+    from ekv_b200 import _lib, shared_prefix as sp
+
+    assert _lib.torch_binding() is not None, "lib/_ekv_torch.so was not built"
+    blocks, rows, lengths, prefixes, table, mapping = _random_case(77, 12, 40, 4, 6, 200, 900, torch.int32)
+    args = dict(source_rows=rows, seq_len=lengths.to(cuda_device), shared_tokens=prefixes, block_size=4,
+                request_table=table.to(cuda_device), device_mapping=mapping.to(cuda_device), exclude_newest=True)
+    dev_blocks = blocks.to(cuda_device)
+    masked_fast = dev_blocks.clone()
+    fast = sp.resolve_shared_block_locations_batched(dev_blocks, **args, masked_block_ids=masked_fast)
+    tuple_rows = sp.resolve_shared_block_locations_batched(dev_blocks, **{**args, "source_rows": tuple(rows)})
+    # The reference accepts only Python ints (shared_prefix.py:150-160): numpy ints and
+    # bools are refused with its message, through the checked path.
+    for bad in (np.array(rows), [True] * 12):
+        with pytest.raises(ValueError, match="source row is outside"):
+            sp.resolve_shared_block_locations_batched(dev_blocks, **{**args, "source_rows": bad})
+    monkeypatch.setattr(sp, "torch_binding", lambda: None)
+    masked_slow = dev_blocks.clone()
+    slow = sp.resolve_shared_block_locations_batched(dev_blocks, **args, masked_block_ids=masked_slow)
+    for a, b, c in zip(fast, slow, tuple_rows):
+        assert torch.equal(a, b) and torch.equal(a, c)
+    assert torch.equal(masked_fast, masked_slow)
