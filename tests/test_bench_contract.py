@@ -1,0 +1,49 @@
+"""The bench.py contract on CPU: one JSON line on stdout with the driver's keys.
+
+The reference arm runs on the host cores (no GPU), so its full output can be checked
+here; the GPU arm's argument parsing is checked without running it.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+from conftest import ROOT
+
+
+def test_reference_arm_prints_one_json_line():
+    env = {**os.environ, "CUDA_VISIBLE_DEVICES": ""}
+    done = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "1"], capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
+    assert done.returncode == 0, done.stderr[-2000:]
+    lines = [line for line in done.stdout.splitlines() if line.strip()]
+    assert len(lines) == 1, done.stdout[-2000:]
+    result = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in result, key
+    assert result["impl"] == "reference" and result["value"] > 0 and result["steps"] == 1
+    assert result["e2e"]["h2d_bytes_per_step"] == 0 and result["e2e"]["d2h_bytes_per_step"] == 0
+    assert result["cpu_baseline"]["kind"] in ("port", "reference") and result["cpu_baseline"]["cores"] >= 1
+    assert "workload" in result["config"]
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    env = {**os.environ, "CUDA_VISIBLE_DEVICES": "", "RANK": "3", "WORLD_SIZE": "4"}
+    done = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "4"],
+                          capture_output=True, text=True, timeout=300, env=env, cwd=ROOT)
+    assert done.returncode == 0 and not done.stdout.strip()
+
+
+def test_bench_arguments():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    args = bench.parse_args([])
+    assert args.gpus == 1 and args.config == 2 and args.impl == "ours" and args.only is None
+    assert args.warmup >= 3
+    args = bench.parse_args(["--gpus", "8", "--steps", "7", "--warmup", "4", "--only", "shadow"])
+    assert (args.gpus, args.steps, args.warmup, args.only) == (8, 7, 4, "shadow")
