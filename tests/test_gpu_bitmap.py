@@ -229,3 +229,26 @@ def test_counts_with_plane_groups_straddles_and_overflow(n_chunks, cuda_device):
     assert int(projection.overflow.item()) == want_overflow
     if n_chunks == 700:
         assert want_overflow > 0  # the last planes run past the table
+
+
+def test_grouped_counts_equal_the_sum_of_single_planes(cuda_device):
+    """A group of planes (one shared histogram) counts exactly what its planes count one at
+    a time through the per-plane kernel, overflow included -- also for negative page ids,
+    which the grouped kernel hands to its inline per-plane path."""
+    from ekv_b200.releasable import ChunkProjection
+
+    gen = torch.Generator().manual_seed(8)
+    n_chunks, chunk_bytes, page_size = 3000, 1024, 5
+    planes = [(0, 200), (700, 200), (1500, 200), (2900, 200)]
+    pages = torch.cat([torch.randint(-3000, 0, (200,), generator=gen), torch.randperm(6000, generator=gen)[:2000]])
+    pages_dev = pages.to(cuda_device)
+    joint = ChunkProjection(planes, page_size, chunk_bytes, n_chunks, cuda_device)
+    got = joint.counts(pages_dev)
+    total = torch.zeros(n_chunks, dtype=torch.int32, device=cuda_device)
+    overflow = 0
+    for plane in planes:
+        single = ChunkProjection([plane], page_size, chunk_bytes, n_chunks, cuda_device)
+        total += single.counts(pages_dev)
+        overflow += int(single.overflow.item())
+    assert torch.equal(got, total)
+    assert int(joint.overflow.item()) == overflow and overflow > 0
