@@ -78,9 +78,10 @@ __device__ __forceinline__ int64_t resolve_row(const GatherParams& p, int64_t r,
         const int64_t logical = load_index(p.request_table, p.table_es, req * p.table_width + pos);
         element = load_index(p.slot_offsets, p.off_es, logical);
     } else if (p.indirect == 2) {
-        // Mapped: the table holds the row's slot in the request's fixed region, -1 if absent.
+        // Mapped: the table holds the row's slot in the request's fixed region, -1 if
+        // absent; a slot past the region reads as absent too (never outside the region).
         const int64_t slot = load_index(p.request_table, p.table_es, req * p.table_width + pos);
-        if (slot < 0) {
+        if (slot < 0 || (slot + 1) * p.width > p.request_stride) {
             valid = false;
             return 0;
         }

@@ -193,7 +193,12 @@ promote_kernel(const __grid_constant__ PromoteParams p) {
         for (int64_t r = sub; r < count; r += per_request) {
             const int32_t slot = p.promo_slot[b * p.promo_row + r];
             const int32_t token = p.miss_list[b * p.list_row + r];
-            if (slot < 0 || token < 0 || token >= p.history_rows_per_request) continue;
+            // A slot outside the request's hot region (or a token outside its history)
+            // is skipped: the copy never leaves the buffers it was given.
+            if (slot < 0 || token < 0 || token >= p.history_rows_per_request ||
+                (static_cast<int64_t>(slot) + 1) * p.row_bytes > p.request_bytes) {
+                continue;
+            }
             const int64_t src_row = (b * p.history_rows_per_request + token) * p.row_bytes;
             const int64_t dst_row = p.sink_bytes + b * p.request_bytes + static_cast<int64_t>(slot) * p.row_bytes;
             for (int plane = 0; plane < p.n_planes; ++plane) {

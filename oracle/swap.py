@@ -57,7 +57,9 @@ def promote_rows(history, hot_rows, miss_list, miss_count, promo, context):
 
 
 def mapped_gather(hot_rows, res_map, topk, lengths):
-    """out[b, i] = hot_rows[b, res_map[b, t]] for t = topk[b, i] valid and resident, else 0."""
+    """out[b, i] = hot_rows[b, res_map[b, t]] for t = topk[b, i] valid and resident, else 0.
+
+    A slot outside the request's hot region (< 0 or >= its capacity) reads as absent."""
     batch, k = topk.shape
     out = np.zeros((batch, k, hot_rows.shape[2]), dtype=hot_rows.dtype)
     for b in range(batch):
@@ -65,6 +67,6 @@ def mapped_gather(hot_rows, res_map, topk, lengths):
             t = int(topk[b, i])
             if 0 <= t < lengths[b]:
                 s = int(res_map[b, t])
-                if s >= 0:
+                if 0 <= s < hot_rows.shape[1]:
                     out[b, i] = hot_rows[b, s]
     return out

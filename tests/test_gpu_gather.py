@@ -199,3 +199,35 @@ def test_bulk_gather_falls_back_for_misaligned_rows(gather_kernel, cuda_device):
                                      table_width=tokens, request_stride=0, sink_elements=0, indirect=True)
     for out, exp in zip(outputs, expected):
         np.testing.assert_array_equal(out.view(torch.int16).cpu().numpy(), exp)
+
+
+def test_mapped_gather_reads_slots_outside_the_region_as_absent(gather_kernel, cuda_device):
+    """Mapped mode (residency map -> slot in the request's fixed hot region): slots < 0 or
+    past the region's capacity give zero rows, never bytes from outside the region."""
+    from ekv_b200.sparse_read import gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+    from oracle import swap as osw
+
+    gen = torch.Generator().manual_seed(17)
+    batch, hot, width, context, k = 3, 64, 128, 500, 40
+    layout = VirtualKVLayout(batch, hot, width, itemsize=2, chunk_bytes=1 << 16)
+    region = layout.request_bytes // 2 // width  # slots per request region (>= hot)
+    planes = [torch.randint(-30000, 30000, (layout.capacity_bytes // 2,), generator=gen, dtype=torch.int16)
+              for _ in range(2)]
+    res_map = torch.full((batch, context), -1, dtype=torch.int32)
+    topk = torch.stack([torch.randperm(context, generator=gen)[:k] for _ in range(batch)]).to(torch.int32)
+    for b in range(batch):
+        res_map[b, topk[b, :20]] = torch.randperm(region, generator=gen)[:20].to(torch.int32)
+        res_map[b, topk[b, 20]] = region          # just past the region
+        res_map[b, topk[b, 21]] = region + 1000   # far past it
+    lengths = torch.full((batch,), context, dtype=torch.int64)
+    outs = [torch.empty((batch, k, width), dtype=torch.int16, device=cuda_device) for _ in range(2)]
+    gather_rows_planes([p.to(cuda_device) for p in planes], topk.to(cuda_device),
+                       torch.arange(batch, device=cuda_device), lengths.to(cuda_device),
+                       res_map.to(cuda_device), None, outs, layout, indirect=False, mapped=True)
+    sink = layout.chunk_bytes // 2
+    for plane, out in zip(planes, outs):
+        hot_rows = plane[sink:].view(batch, region, width).numpy()
+        want = osw.mapped_gather(hot_rows, res_map.numpy(), topk.numpy(), lengths.numpy())
+        np.testing.assert_array_equal(out.cpu().numpy(), want)
+        assert not out[:, 20:22].any()  # the out-of-region slots read as zero rows
