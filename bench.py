@@ -72,7 +72,7 @@ def parse_args(argv=None):
     p.add_argument("--skip-migration", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
-    p.add_argument("--only", choices=("lookup", "shadow", "bitmap"), default=None,
+    p.add_argument("--only", choices=("lookup", "shadow", "bitmap", "roundtrip"), default=None,
                    help="measurement aid: run one side leg alone (no config-2 pool) and print its JSON")
     p.add_argument("--tp-shard", type=int, default=0,
                    help="measurement aid: gather one rank's head shard of TP=N on this GPU "
@@ -430,6 +430,63 @@ def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
 
 
 # --------------------------------------------------------------------------- lookups (config 1, R1)
+
+REFERENCE_ROUND_TRIP = dict(bytes=503_347_200, seconds=0.1314, gbs=3.8,
+                            source="results/vmm-roundtrip-shadow/results.json:699-700 (4x A100, TP4, per rank)")
+
+
+def round_trip_bench(dev, reps=3, spare_chunks=0):
+    """A forced demote + promote round trip through the reference's transaction API
+    (prepare_demote -> commit_demote -> prepare_promote -> commit_promote,
+    adaptive_sparse/migration.py:67-288) on one TP4 rank's shard: 48 layers x K,V of
+    2 KV heads x 128 (512 B rows), page size 64, one request of 5120 committed tokens
+    = 503 MB moved per round trip (the reference's published case moved 503,347,200 B).
+    Wall time includes every sync, the chunk reclaim of the demotion and the chunk
+    commit of the promotion, as the reference's figure does.  The SGLang objects are
+    the package's stand-in (ekv_b200.standin); rows are checked bit for bit."""
+    from ekv_b200 import migration
+    from ekv_b200.standin import install_request, migration_world
+
+    world = migration_world(dev, layers=48, heads=2, head_dim=128, page_size=64, pages=2048, host_rows=8192,
+                            spare_chunks=spare_chunks)
+    try:
+        c = world.coordinator
+        length = 5120
+        req, slots, logical = install_request(world, 1, length)
+        original = [view[slots].clone() for view in world.views]
+        moved = length * 2 * world.layers * world.row_bytes  # per direction
+        samples = []
+        metric_keys = ("ensure_ns", "reclaim_ns", "reclaim_sync_ns", "ensure_chunks", "reclaim_chunks")
+        for _ in range(reps):
+            before = {k: world.backing.metrics[k] for k in metric_keys}
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            prepared = migration.prepare_demote(c, req, torch.cuda.synchronize)
+            released = migration.commit_demote(prepared, lambda row: None, torch.cuda.synchronize,
+                                               trim_quiescent=world.tracker.trim_quiescent)
+            t1 = time.perf_counter()
+            promoted = migration.prepare_promote(c, req, torch.cuda.synchronize)
+            migration.commit_promote(promoted, lambda row: None, torch.cuda.synchronize)
+            torch.cuda.synchronize()
+            t2 = time.perf_counter()
+            after = world.backing.metrics
+            samples.append((t1 - t0, t2 - t1, t2 - t0, released, {k: after[k] - before[k] for k in metric_keys}))
+        destination = world.pool.full_to_hisparse_device_index_mapping[logical]
+        exact = all(bool(torch.equal(view[destination], want)) for view, want in zip(world.views, original))
+        demote_s, promote_s, total_s, released, vmm = min(samples, key=lambda x: x[2])
+        ref = REFERENCE_ROUND_TRIP
+        return {"tokens": length, "layers": world.layers, "row_bytes": world.row_bytes,
+                "bytes_round_trip": 2 * moved, "demote_ms": demote_s * 1e3, "promote_ms": promote_s * 1e3,
+                "round_trip_ms": total_s * 1e3, "gbs_combined": 2 * moved / total_s / 1e9,
+                "round_trip_ms_median": statistics.median(x[2] for x in samples) * 1e3,
+                "released_bytes_per_demotion": released, "bit_exact": exact, "spare_chunks": spare_chunks,
+                "vmm": {"commit_ms": vmm["ensure_ns"] / 1e6, "reclaim_ms": vmm["reclaim_ns"] / 1e6,
+                        "reclaim_sync_ms": vmm["reclaim_sync_ns"] / 1e6, "chunks_committed": vmm["ensure_chunks"],
+                        "chunks_reclaimed": vmm["reclaim_chunks"]},
+                "reference_published": ref, "vs_reference_published": (2 * moved / total_s / 1e9) / ref["gbs"]}
+    finally:
+        world.close()
+
 
 def commit_path_bench(work, victims, segments, planes, dst, host, plane_index, shadow, dense, batch=32,
                       rounds=3):
@@ -960,6 +1017,8 @@ def run_ours(args, dist: Dist):
         result["cpu_baseline"] = cpu_baseline(work, args.cpu_seconds)
     if dist.world == 1 and not args.skip_migration:
         result["migration"] = migration_bench(work)
+        result["migration"]["round_trip"] = round_trip_bench(dist.device)
+        result["migration"]["round_trip_spare_handles"] = round_trip_bench(dist.device, spare_chunks=256)
     work.close()
     return result
 
@@ -1373,6 +1432,9 @@ def main(argv=None):
         if args.only:
             if args.only == "bitmap":
                 leg_result = bitmap_bench(dist, shard=args.tp_shard)
+            elif args.only == "roundtrip":
+                leg_result = {"plain": round_trip_bench(dist.device),
+                              "spare_handles": round_trip_bench(dist.device, spare_chunks=256)}
             else:
                 leg_result = {"lookup": lookup_bench, "shadow": shadow_bench}[args.only](dist)
             result = {"leg": args.only, **leg_result}
