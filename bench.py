@@ -14,7 +14,9 @@ host memory and one result row read back), ``roofline`` (gather kernel vs the
 measured HBM copy peak), ``cpu_baseline`` (torch-CPU restatement on the host
 cores, bounded sample), ``migration`` (config 3: 256 victim chunks packed into
 pinned host staging through the copy-engine ring and restored into fresh VMM
-chunks with permuted slots; host-link GB/s per direction), ``lookup``
+chunks with permuted slots; host-link GB/s per direction; plus the commit path and a
+forced demote + promote round trip through the transaction API at the size of the
+reference's published case), ``lookup``
 (config 1 lookups, resolve_resident at the reference's microbenchmark shape,
 shared-prefix donor resolution at the config-5 shape), ``shadow`` (logical-shadow
 bitwise check of one decode step at the config-2 batch, vs the reference's torch body
