@@ -4,6 +4,8 @@ from __future__ import annotations
 
 import ctypes as ct
 import re
+
+import pytest
 from conftest import ROOT
 
 _DECL = re.compile(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*\b((?:ekv|ev)_[a-z0-9_]+)\s*\(",
@@ -61,3 +63,27 @@ def test_entry_points_validate_before_touching_a_device(library_path):
 
     if not torch.cuda.is_available():
         assert not lib.ev_create(0, 1 << 21, 1 << 21) and lib.ev_error()
+
+
+def test_compiled_binding_loads_and_declines_cpu_tensors(library_path):
+    """lib/_ekv_torch.so (built with the library) loads without a GPU; for CPU tensors it
+    reports NOT_HANDLED, so the Python API's checks run and raise its own errors."""
+    import torch
+
+    from ekv_b200 import _lib
+    from ekv_b200.resident_lookup import lookup_slots, resolve_resident
+
+    binding = _lib.torch_binding()
+    if binding is None:
+        pytest.skip("the torch binding was not built here")
+    topk = torch.zeros((1, 2, 4), dtype=torch.int32)
+    args = (topk, torch.zeros((2, 8), dtype=torch.int64), torch.zeros(9, dtype=torch.int64), torch.arange(2),
+            torch.full((2,), 8), torch.arange(2), torch.zeros((1, 2, 4), dtype=torch.int32), 1)
+    assert binding.resolve_resident(*args) == binding.NOT_HANDLED
+    status, *_ = binding.lookup_slots(torch.zeros((2, 8), dtype=torch.int32), torch.zeros((2, 4), dtype=torch.int32),
+                                      None, None, None, None, None, True)
+    assert status == binding.NOT_HANDLED
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        resolve_resident(*args)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        lookup_slots(torch.zeros((2, 8), dtype=torch.int32), torch.zeros((2, 4), dtype=torch.int32))
