@@ -115,3 +115,53 @@ def test_spare_handles_are_reused_and_zeroed(cuda_device):
     finally:
         torch.cuda.synchronize()
         backing.close()  # releases the kept handles too
+
+
+def test_captured_gather_survives_reclaim_and_recommit(cuda_device):
+    """A CUDA graph captured over the VMM-backed pool keeps working across a reclaim and a
+    recommit of one chunk: the virtual addresses it captured stay valid, rows that avoid
+    the reclaimed chunk still gather, and after the recommit the chunk reads as its new
+    contents (as tests/test_graph_backing.py:9-51 of the reference checks for index_select)."""
+    from ekv_b200.backing import Backing
+    from ekv_b200.sparse_read import PlaneGather
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    layout = VirtualKVLayout(2, 2048, 512, itemsize=2, chunk_bytes=CHUNK)  # one chunk per request region
+    backing = Backing(layout.capacity_bytes, CHUNK, device=cuda_device.index)
+    try:
+        backing.ensure({0, 1, 2})
+        plane = backing.raw.view(torch.int16)
+        base = backing.raw.data_ptr()
+        rows = plane[CHUNK // 2:].view(2, 2048, 512)
+        rows[0] = torch.arange(2048, device=cuda_device, dtype=torch.int16)[:, None]
+        rows[1] = -torch.arange(2048, device=cuda_device, dtype=torch.int16)[:, None]
+        positions = torch.tensor([[5, 9, 2047, 0], [7, 1, 100, 3]], dtype=torch.int64, device=cuda_device)
+        request_ids = torch.tensor([0, 1], dtype=torch.int64, device=cuda_device)
+        lengths = torch.tensor([2048, 2048], dtype=torch.int64, device=cuda_device)
+        out = torch.empty((2, 4, 512), dtype=torch.int16, device=cuda_device)
+        gather = PlaneGather([plane], positions, request_ids, lengths, None, None, [out], layout, indirect=False)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            gather()
+
+        def replay(pos, want_first):
+            positions.copy_(torch.tensor(pos, dtype=torch.int64, device=cuda_device))
+            graph.replay()
+            torch.cuda.synchronize()
+            assert out[:, :, 0].tolist() == want_first
+            assert backing.raw.data_ptr() == base
+
+        replay([[5, 9, 2047, 0], [7, 1, 100, 3]], [[5, 9, 2047, 0], [-7, -1, -100, -3]])
+        assert backing.reclaim({2}) == 1 and backing.mapped_chunks == {0, 1}
+        # Request 1's rows are invalid (-1): they read as zeros without touching its chunk.
+        replay([[4, 3, 2, 1], [-1, -1, -1, -1]], [[4, 3, 2, 1], [0, 0, 0, 0]])
+        assert backing.ensure({2}) == 1
+        rows = backing.raw.view(torch.int16)[CHUNK // 2:].view(2, 2048, 512)
+        assert not rows[1].any()  # recommitted memory is zero-filled
+        rows[1] = 3000
+        replay([[1, 1, 1, 1], [0, 5, 2047, 9]], [[1, 1, 1, 1], [3000, 3000, 3000, 3000]])
+        del graph, plane, rows
+    finally:
+        torch.cuda.synchronize()
+        backing.close()
