@@ -1034,7 +1034,9 @@ def run_config4(args, dist: Dist):
     hot-slot lookup (R2) of that layer's Top-K followed by the gather of the hits from
     the layer's fixed-position hot pool (direct addressing, misses read as zero rows);
     then the freeable-bitmap AND-combine across ranks.  The 96 launches of a step are
-    replayed from one CUDA graph."""
+    replayed from one CUDA graph in plain layer order (the reported value); the same
+    launches with layer i's gather overlapping layer i+1's lookup (``LayerPipeline``)
+    are timed beside it."""
     import numpy as np
 
     from ekv_b200.resident_lookup import LookupPlan
@@ -1079,12 +1081,19 @@ def run_config4(args, dist: Dist):
         gathers.append(PlaneGather(planes[2 * layer:2 * layer + 2], plan.slots, req_ids, lengths, None, None,
                                    [out_k, out_v], layout, indirect=False))
 
-    def layers_step():
+    from ekv_b200.pipeline import LayerPipeline
+
+    pipeline = LayerPipeline(lookups, gathers, dev)
+
+    def layers_step(overlap=True):
+        if overlap:  # layer i's gather on a second stream while layer i+1's lookup runs
+            pipeline()
+            return
         for layer in range(layers):
             lookups[layer]()
             gathers[layer]()
 
-    layers_step()
+    layers_step(False)
     torch.cuda.synchronize()
     # Parity on layer 0 (and the last layer) against the oracle, on this rank's head shard.
     parity = True
@@ -1101,18 +1110,30 @@ def run_config4(args, dist: Dist):
                                   table_width=hot, request_stride=layout.request_bytes // 2,
                                   sink_elements=CHUNK // 2, indirect=False)
             parity &= np.array_equal(out.view(torch.int16).cpu().numpy(), want)
-    graph = None
+    # The pipelined step leaves the last layer's rows in the outputs, as the plain one.
+    layers_step(False)
+    torch.cuda.synchronize()
+    plain_out = (out_k.clone(), out_v.clone())
+    out_k.zero_()
+    out_v.zero_()
+    layers_step(True)
+    torch.cuda.synchronize()
+    parity &= bool(torch.equal(out_k, plain_out[0]) and torch.equal(out_v, plain_out[1]))
+    del plain_out
+    graphs = {}
     try:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
-            layers_step()
+            layers_step(True)
+            layers_step(False)
         torch.cuda.current_stream(dev).wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            layers_step()
+        for overlap in (True, False):
+            graphs[overlap] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graphs[overlap]):
+                layers_step(overlap)
     except Exception as exc:  # capture unsupported: time eager launches instead
-        graph = None
+        graphs = {}
         capture_error = str(exc)
     else:
         capture_error = None
@@ -1122,16 +1143,18 @@ def run_config4(args, dist: Dist):
 
     local = torch.zeros(64, dtype=torch.int64, device=dev)
 
-    def step():
-        if graph is not None:
-            graph.replay()
+    def step(overlap):
+        if graphs:
+            graphs[overlap].replay()
         else:
-            layers_step()
+            layers_step(overlap)
         combine_freeable(local)
 
     with ClockSampler(dist.local_rank) as clocks:
-        ms = timed(step, args.steps, args.warmup, dist)
+        ms = timed(lambda: step(False), args.steps, args.warmup, dist)
+        pipelined_ms = timed(lambda: step(True), args.steps, args.warmup, dist)
     ms_per_step = ms / args.steps
+    pipelined_ms_per_step = pipelined_ms / args.steps
     units = reqs * k * layers
     hits = reqs * n_hits * layers
     bytes_per_step = hits * 4 * row_bytes + units * (4 + 4 + 4 + 1)  # payload + lookup traffic
@@ -1146,7 +1169,13 @@ def run_config4(args, dist: Dist):
                                f"{reqs} requests x {ctx} context, hot {hot}/request, Top-K {k}, "
                                f"heads {heads}/rank, bitmap AND-combine per step",
                    "parallelism": f"tp{dist.world} (KV-head sharding; lookup replicated; NCCL AND-combine)",
-                   "cuda_graph": graph is not None, "capture_error": capture_error},
+                   "cuda_graph": bool(graphs), "capture_error": capture_error},
+        "pipelined": {"ms_per_step": pipelined_ms_per_step, "value": units / (pipelined_ms_per_step / 1e3),
+                      "speedup": ms_per_step / pipelined_ms_per_step,
+                      "what": "LayerPipeline: layer i's gather on a second stream while layer i+1's lookup "
+                              "runs; valid only when every layer's Top-K is known when the step starts "
+                              "(a per-layer indexer makes layer i+1's Top-K depend on layer i), so the "
+                              "reported value is the plain layer order"},
         "hbm_gbs_per_gpu": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_source,
@@ -1156,7 +1185,7 @@ def run_config4(args, dist: Dist):
         "gpu_launches": 2 * layers * args.steps + args.steps * (dist.world > 1),
         "clocks": clocks.summary(),
     }
-    del graph
+    graphs.clear()
     return result
 
 
@@ -1352,7 +1381,9 @@ def run_config5(args, dist: Dist):
         "sequential_ms_per_step": sequential_ms_per_step,
         "overlap_speedup": sequential_ms_per_step / ms_per_step,
         "timing": "even steps overlapped (SwapPipeline: layer i's gather on a second stream during layer "
-                  "i+1's promotion) = the reported value; odd steps in plain layer order = sequential_ms_per_step",
+                  "i+1's promotion) = the reported value; odd steps in plain layer order = sequential_ms_per_step; "
+                  "the overlap is valid because a step's one Top-K set (copied in before the layers) serves "
+                  "every layer, so no layer's swap-in waits on an earlier layer",
         "promoted_rows_per_step": promoted_rows / all_steps,
         "promoted_bytes_per_step": promoted_bytes_step,
         "host_link_gbs": promoted_bytes_step / (ms_per_step / 1e3) / 1e9,

@@ -1,0 +1,50 @@
+"""Two-stream layer pipeline for one decode step.
+
+A decode step runs, per layer, a short producer (the residency lookup, or the
+lookup + victim selection + promotion of a host-backed request) followed by
+the HBM-bound gather that reads the producer's output.  Layer i+1's producer
+does not depend on layer i's gather, so the two can run at the same time when
+the producer's blocks fit on the SMs beside the gather's (register and shared
+memory budgets are sized for that: the gather leaves room for one producer
+block per SM).
+
+``LayerPipeline`` runs the producers in layer order on the caller's stream and
+the consumers in layer order on a second stream, with one event per layer
+between them; the caller's stream waits for the last consumer before the call
+returns.  Consumers stay ordered among themselves, so the layers may share one
+output buffer.  It works eagerly and under CUDA graph capture (the second
+stream forks from and joins the caller's stream).
+"""
+
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import torch
+
+Launch = Callable[[int], None]
+
+
+class LayerPipeline:
+    """``produce[i](stream)`` then ``consume[i](stream)`` for every layer, with
+    consumer i overlapping producer i+1 (see module docstring)."""
+
+    def __init__(self, produce: Sequence[Launch], consume: Sequence[Launch], device):
+        self.produce, self.consume = list(produce), list(consume)
+        if not self.produce or len(self.produce) != len(self.consume):
+            raise ValueError("need one producer and one consumer per layer, at least one layer")
+        self.device = torch.device(device)
+        self.side = torch.cuda.Stream(self.device)
+        self.ready = [torch.cuda.Event() for _ in self.produce]
+
+    def __call__(self) -> None:
+        main = torch.cuda.current_stream(self.device)
+        side = self.side
+        side.wait_stream(main)  # fork: the consumers see everything issued before the step
+        main_handle, side_handle = main.cuda_stream, side.cuda_stream
+        for produce, consume, ready in zip(self.produce, self.consume, self.ready):
+            produce(main_handle)
+            ready.record(main)
+            side.wait_event(ready)
+            consume(side_handle)
+        main.wait_stream(side)  # join

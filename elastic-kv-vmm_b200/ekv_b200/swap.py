@@ -22,6 +22,7 @@ from __future__ import annotations
 import torch
 
 from ._lib import MAX_PLANES, call, require_cuda, stream_handle, u64_array
+from .pipeline import LayerPipeline
 from .resident_lookup import LookupPlan
 from .sparse_read import PlaneGather
 from .virtual_layout import VirtualKVLayout
@@ -158,7 +159,7 @@ class SwapStep:
         self.gather(stream)
 
 
-class SwapPipeline:
+class SwapPipeline(LayerPipeline):
     """All layers of a decode step with each layer's gather overlapped with the next
     layer's swap-in.
 
@@ -178,18 +179,4 @@ class SwapPipeline:
         self.plans = list(plans)
         if not self.plans:
             raise ValueError("need at least one layer")
-        self.device = self.plans[0].device
-        self.side = torch.cuda.Stream(self.device)
-        self.ready = [torch.cuda.Event() for _ in self.plans]
-
-    def __call__(self) -> None:
-        main = torch.cuda.current_stream(self.device)
-        side = self.side
-        side.wait_stream(main)  # fork: the gathers see everything issued before the step
-        main_handle, side_handle = main.cuda_stream, side.cuda_stream
-        for plan, ready in zip(self.plans, self.ready):
-            plan.swap_in(main_handle)
-            ready.record(main)
-            side.wait_event(ready)
-            plan.gather(side_handle)
-        main.wait_stream(side)  # join
+        super().__init__([p.swap_in for p in self.plans], [p.gather for p in self.plans], self.plans[0].device)

@@ -231,3 +231,73 @@ def test_mapped_gather_reads_slots_outside_the_region_as_absent(gather_kernel, c
         want = osw.mapped_gather(hot_rows, res_map.numpy(), topk.numpy(), lengths.numpy())
         np.testing.assert_array_equal(out.cpu().numpy(), want)
         assert not out[:, 20:22].any()  # the out-of-region slots read as zero rows
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_layer_pipeline_lookup_then_gather(graph, gather_kernel, cuda_device):
+    """LayerPipeline over per-layer (lookup, direct gather) pairs -- the config-4 decode
+    step with layer i's gather overlapping layer i+1's lookup -- gives every layer's
+    rows exactly as the oracle's lookup + gather; with ``graph`` it is captured once
+    and replayed."""
+    from ekv_b200.pipeline import LayerPipeline
+    from ekv_b200.resident_lookup import LookupPlan
+    from ekv_b200.sparse_read import PlaneGather
+    from ekv_b200.virtual_layout import VirtualKVLayout
+    from oracle import lookup as ol
+
+    dev = cuda_device
+    gen = torch.Generator().manual_seed(29)
+    layers, batch, context, hot, k, width = 5, 6, 3000, 256, 200, 128
+    layout = VirtualKVLayout(batch, hot, width, itemsize=2, chunk_bytes=1 << 16)
+    req_ids = torch.arange(batch, device=dev)
+    lengths = torch.full((batch,), hot, dtype=torch.int64, device=dev)
+    maps, topks, planes, outs, lookups, gathers = [], [], [], [], [], []
+    for _ in range(layers):
+        res_map = torch.full((batch, context), -1, dtype=torch.int32)
+        topk = torch.empty((batch, k), dtype=torch.int32)
+        for b in range(batch):
+            perm = torch.randperm(context, generator=gen)
+            res_map[b, perm[:hot]] = torch.randperm(hot, generator=gen).to(torch.int32)
+            topk[b] = torch.cat([perm[:150], perm[hot:hot + k - 150]])[torch.randperm(k, generator=gen)].to(torch.int32)
+        maps.append(res_map)
+        topks.append(topk)
+        layer_planes = [torch.randint(-30000, 30000, (layout.capacity_bytes // 2,), generator=gen,
+                                      dtype=torch.int16) for _ in range(2)]
+        planes.append(layer_planes)
+        layer_outs = [torch.full((batch, k, width), 7, dtype=torch.int16, device=dev) for _ in range(2)]
+        outs.append(layer_outs)
+        plan = LookupPlan(res_map.to(dev), topk.to(dev))
+        lookups.append(plan)
+        gathers.append(PlaneGather([p.to(dev).view(torch.bfloat16) for p in layer_planes], plan.slots, req_ids,
+                                   lengths, None, None, [o.view(torch.bfloat16) for o in layer_outs], layout,
+                                   indirect=False))
+    pipeline = LayerPipeline(lookups, gathers, dev)
+    if graph:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            pipeline()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        for layer_outs in outs:
+            for o in layer_outs:
+                o.fill_(7)
+        replay = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(replay):
+            pipeline()
+        replay.replay()
+    else:
+        pipeline()
+    torch.cuda.synchronize()
+    for layer in range(layers):
+        slots, _, _, _ = ol.lookup_slots(maps[layer].numpy(), topks[layer].numpy())
+        np.testing.assert_array_equal(lookups[layer].slots.cpu().numpy(), slots)
+        want = og.gather_rows_planes([p.numpy() for p in planes[layer]], slots, req_ids.cpu().numpy(),
+                                     lengths.cpu().numpy(), None, None, width=width, table_width=hot,
+                                     request_stride=layout.request_bytes // 2,
+                                     sink_elements=layout.chunk_bytes // 2, indirect=False)
+        for out, exp in zip(outs[layer], want):
+            np.testing.assert_array_equal(out.cpu().numpy(), exp)
+    if graph:
+        del replay
+

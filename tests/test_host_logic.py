@@ -558,3 +558,12 @@ def test_logical_shadow_host_contract(tmp_path):
     shadow.dirty = True
     with pytest.raises(RuntimeError, match="Logical KV shadow mismatch"):
         shadow.publish(tmp_path, 2)
+
+
+def test_layer_pipeline_contract():
+    from ekv_b200.pipeline import LayerPipeline
+
+    with pytest.raises(ValueError, match="one producer and one consumer"):
+        LayerPipeline([], [], "cpu")
+    with pytest.raises(ValueError, match="one producer and one consumer"):
+        LayerPipeline([lambda s: None], [], "cpu")
