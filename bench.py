@@ -647,6 +647,7 @@ def lookup_bench(dist: Dist, rounds: int = 20, calls: int = 100):
     resolve_us = p50(resolve_call)
     resolve_graph_us = graph_us(resolve_call)
     shared = shared_prefix_bench(dev, p50, graph_us)
+    gather_api = gather_api_bench(dev, p50, graph_us)
     expected = torch.tensor([[((rb - 1 - r) * 8192 + blk * 512 + off + 1) * 3 + 5
                               for blk in range(16) for off in range(128)] for r in range(rb)],
                             dtype=torch.int32, device=dev)
@@ -659,9 +660,60 @@ def lookup_bench(dist: Dist, rounds: int = 20, calls: int = 100):
             "resolve_resident_batch4_device_us": resolve_graph_us,
             "resolve_resident_published_a100_triton_us": 30.08,
             "resolve_resident_correct": bool(torch.equal(result[0], expected)),
-            "shared_prefix": shared,
+            "shared_prefix": shared, "gather_rows_api": gather_api,
             "timing": "p50 of per-call CUDA-event time, 100 calls per round (reference methodology, "
                       "includes host dispatch); *_device_us: the same 100 calls replayed from one CUDA graph"}
+
+
+def gather_api_bench(dev, p50, graph_us):
+    """The reference's single-plane ``gather_rows`` call (indirect addressing) at one
+    layer's K plane of config 2 under TP8 (64 requests x 2048 rows of 256 B): time per
+    call through the public API (compiled binding, and the ctypes path with the binding
+    hidden) against the kernel's device time (CUDA graph)."""
+    from ekv_b200 import sparse_read
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    batch, rows, width = 64, 2048, 128
+    layout = VirtualKVLayout(batch, rows, width, itemsize=2, chunk_bytes=CHUNK)
+    gen = torch.Generator(device=dev).manual_seed(12)
+    raw = torch.empty(layout.capacity_bytes // 2, dtype=torch.bfloat16, device=dev)
+    torch.randn(raw.shape, generator=gen, dtype=torch.bfloat16, device=dev, out=raw)
+    slots = (layout.capacity_bytes // 2 - layout.chunk_bytes // 2) // width
+    positions = torch.stack([torch.randperm(rows, generator=gen, device=dev) for _ in range(batch)])
+    request_ids = torch.arange(batch, device=dev)
+    lengths = torch.full((batch,), rows, dtype=torch.int64, device=dev)
+    table = torch.arange(batch * rows, device=dev).view(batch, rows)
+    offsets = layout.chunk_bytes // 2 + torch.randperm(slots, generator=gen, device=dev)[:batch * rows] * width
+    out = torch.empty((batch, rows, width), dtype=torch.bfloat16, device=dev)
+
+    def call():
+        sparse_read.gather_rows(raw, positions, request_ids, lengths, table, offsets, out, layout, indirect=True)
+
+    def host_us(calls=50, rounds=10):
+        """Host time per call (the launches queue up; the device is not waited for)."""
+        samples = []
+        for _ in range(rounds):
+            torch.cuda.synchronize()
+            start = time.perf_counter()
+            for _ in range(calls):
+                call()
+            samples.append((time.perf_counter() - start) * 1e6 / calls)
+        torch.cuda.synchronize()
+        return statistics.median(samples)
+
+    api_us, api_host_us = p50(call), host_us()
+    device_us = graph_us(call)
+    binding = sparse_read.torch_binding
+    sparse_read.torch_binding = lambda: None
+    try:
+        ctypes_us, ctypes_host_us = p50(call), host_us()
+    finally:
+        sparse_read.torch_binding = binding
+    return {"api_us": api_us, "host_us": api_host_us, "ctypes_api_us": ctypes_us, "ctypes_host_us": ctypes_host_us,
+            "device_us": device_us, "binding": binding() is not None, "rows": batch * rows,
+            "row_bytes": width * 2,
+            "timing": "api_us: p50 CUDA-event time per call of 100 back-to-back calls (the slower of host "
+                      "and device); host_us: host time per call; device_us: CUDA-graph replay"}
 
 
 def shared_prefix_bench(dev, p50, graph_us):

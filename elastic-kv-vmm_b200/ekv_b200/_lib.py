@@ -214,7 +214,7 @@ TORCH_BINDING_PATH = LIBRARY_PATH.parent / "_ekv_torch.so"
 
 @functools.lru_cache(maxsize=None)
 def torch_binding():
-    """The compiled pybind11 binding of the per-call lookups, or None.
+    """The compiled pybind11 binding of the per-call lookups and gathers, or None.
 
     It calls the same C entry points of the library loaded above (their
     addresses are handed over here), reading tensor pointers and strides in C++
@@ -234,7 +234,9 @@ def torch_binding():
     lib = library()
     module.bind(ct.cast(lib.ekv_resolve_resident, ct.c_void_p).value,
                 ct.cast(lib.ekv_lookup_slots, ct.c_void_p).value,
-                ct.cast(lib.ekv_resolve_shared_blocks, ct.c_void_p).value)
+                ct.cast(lib.ekv_resolve_shared_blocks, ct.c_void_p).value,
+                ct.cast(lib.ekv_gather_rows, ct.c_void_p).value,
+                ct.cast(lib.ekv_gather_rows_planes, ct.c_void_p).value)
     return module
 
 

@@ -1,6 +1,8 @@
 // Error state, device binding and launch sizing shared by every entry point.
 #include "common.cuh"
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -40,6 +42,14 @@ int persistent_grid(const void* kernel, int threads, size_t smem, int device) {
                "occupancy query");
     if (per_sm < 1) per_sm = 1;
     return per_sm * sm_count(device);
+}
+
+bool dependent_launch_enabled() {
+    static const bool enabled = [] {
+        const char* value = std::getenv("EKV_B200_PDL");
+        return !(value && std::strcmp(value, "0") == 0);
+    }();
+    return enabled;
 }
 
 }  // namespace ekv

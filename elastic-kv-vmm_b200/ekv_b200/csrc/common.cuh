@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #include "../../../include/ekv_kernels.h"
 
@@ -62,6 +63,33 @@ inline void check_launch(const char* what) {
     cuda_check(cudaGetLastError(), what);
 }
 
+// Whether kernels of a decode step are launched as programmatic dependents of
+// the work before them in their stream (EKV_B200_PDL=0 turns it off).
+bool dependent_launch_enabled();
+
+// Launch `kernel` as a programmatic dependent of the previous work in `stream`:
+// its blocks may be scheduled while that work finishes (once every block of a
+// preceding kernel has called allow_dependents() or exited), which hides the
+// launch latency between the short per-layer kernels of a decode step.  The
+// kernel must call grid_dependency_wait() before its first global memory
+// access; that wait returns when the preceding grids have completed and their
+// writes are visible.
+template <typename... Params, typename... Args>
+void launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      const char* what, Args&&... args) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = dependent_launch_enabled() ? 1 : 0;
+    cuda_check(cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...), what);
+}
+
 // ---------------------------------------------------------------- device side
 
 // Read element i of a signed int32 / int64 array.
@@ -71,6 +99,14 @@ __device__ __forceinline__ int64_t load_index(const void* base, int esize, int64
 }
 
 __device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
+
+// Programmatic dependent launch, device side.  grid_dependency_wait(): block
+// until the grids this one was launched behind have completed and their memory
+// is visible (immediate for an ordinary launch).  allow_dependents(): let the
+// next kernel of the stream start scheduling its blocks; it still waits for
+// this grid to complete before reading anything.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Lowest power of two (<= 16) dividing x.
 __device__ __forceinline__ int64_t alignment_of(uint64_t x) {

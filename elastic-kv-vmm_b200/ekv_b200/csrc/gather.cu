@@ -220,6 +220,8 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
 // of all planes with the offset broadcast from its lane.
 __global__ void __launch_bounds__(kGatherThreads, kGatherBlocksPerSM)
 gather_kernel(const __grid_constant__ GatherParams p) {
+    grid_dependency_wait();
+    allow_dependents();
     const int64_t n_rows = p.batch * p.selected;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
     const unsigned lane = lane_id();
@@ -518,7 +520,8 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
             const unsigned grid = static_cast<unsigned>(needed < sms ? needed : sms);
             gather_bulk_kernel<<<grid, kBulkThreads, shape.smem, s>>>(p, shape.slots, shape.slot_bytes);
         } else {
-            gather_kernel<<<gather_grid(device, n_rows), kGatherThreads, 0, s>>>(p);
+            launch_dependent(gather_kernel, dim3(gather_grid(device, n_rows)), dim3(kGatherThreads), 0, s,
+                             "gather_rows launch", p);
         }
         check_launch("gather_rows launch");
     });

@@ -39,6 +39,8 @@ constexpr int kResolveItems = 4;  // independent lookup chains per thread
 // grid.y walks the selected rows.
 __global__ void __launch_bounds__(kResolveThreads)
 resolve_kernel(const __grid_constant__ ResolveParams p) {
+    grid_dependency_wait();
+    allow_dependents();
     for (int64_t s = blockIdx.y; s < p.n_selected; s += gridDim.y) {
         const int64_t row = load_index(p.selected, p.sel_es, s * p.sel_stride);
         const int64_t length = load_index(p.lengths, p.len_es, row * p.len_stride);
@@ -123,6 +125,8 @@ constexpr int kLookupWarps = kLookupThreads / 32;
 template <int kItems>
 __global__ void __launch_bounds__(kLookupThreads, EKV_LOOKUP_MIN_BLOCKS)
 lookup_kernel(const __grid_constant__ LookupParams p) {
+    grid_dependency_wait();
+    allow_dependents();
     constexpr int kLookupItems = kItems;
     constexpr int kLookupTile = kLookupThreads * kItems;
     __shared__ int warp_totals[kLookupWarps];
@@ -257,8 +261,8 @@ extern "C" int ekv_resolve_resident(
         const int64_t gx = (width + tile - 1) / tile;
         require(gx <= 0x7fffffff, "width too large");
         const unsigned gy = static_cast<unsigned>(n_selected < 65535 ? n_selected : 65535);
-        resolve_kernel<<<dim3(static_cast<unsigned>(gx), gy), kResolveThreads, 0,
-                         static_cast<cudaStream_t>(stream)>>>(p);
+        launch_dependent(resolve_kernel, dim3(static_cast<unsigned>(gx), gy), dim3(kResolveThreads), 0,
+                         static_cast<cudaStream_t>(stream), "resolve_resident launch", p);
         check_launch("resolve_resident launch");
     });
 }
@@ -304,13 +308,9 @@ extern "C" int ekv_lookup_slots(
         p.len_es = lengths ? lengths_esize : 4;
         const unsigned grid = static_cast<unsigned>(batch < (1 << 20) ? batch : (1 << 20));
         const auto cstream = static_cast<cudaStream_t>(stream);
-        if (k <= kLookupThreads) {
-            lookup_kernel<1><<<grid, kLookupThreads, 0, cstream>>>(p);
-        } else if (k <= 2 * kLookupThreads) {
-            lookup_kernel<2><<<grid, kLookupThreads, 0, cstream>>>(p);
-        } else {
-            lookup_kernel<4><<<grid, kLookupThreads, 0, cstream>>>(p);
-        }
+        auto* kernel = k <= kLookupThreads ? lookup_kernel<1> : k <= 2 * kLookupThreads ? lookup_kernel<2>
+                                                                                         : lookup_kernel<4>;
+        launch_dependent(kernel, dim3(grid), dim3(kLookupThreads), 0, cstream, "lookup_slots launch", p);
         check_launch("lookup_slots launch");
     });
 }

@@ -69,6 +69,8 @@ __device__ __forceinline__ int64_t clamp64(int64_t v, int64_t lo, int64_t hi) {
 template <int kInline>
 __global__ void __launch_bounds__(kSharedThreads)
 shared_blocks_kernel(const __grid_constant__ SharedLaunch<kInline> launch) {
+    grid_dependency_wait();
+    allow_dependents();
     const SharedParams& p = launch.p;
     const unsigned lane = lane_id();
     const int group = 1 << p.group_log2;
@@ -216,11 +218,13 @@ extern "C" int ekv_resolve_shared_blocks(
                 launch.rows[r] = source_rows[r];
                 launch.prefixes[r] = shared_tokens[r];
             }
-            shared_blocks_kernel<kSharedInline><<<grid, kSharedThreads, 0, cstream>>>(launch);
+            launch_dependent(shared_blocks_kernel<kSharedInline>, dim3(grid), dim3(kSharedThreads), 0, cstream,
+                             "shared_blocks launch", launch);
         } else {
             SharedLaunch<0> launch{};
             launch.p = p;
-            shared_blocks_kernel<0><<<grid, kSharedThreads, 0, cstream>>>(launch);
+            launch_dependent(shared_blocks_kernel<0>, dim3(grid), dim3(kSharedThreads), 0, cstream,
+                             "shared_blocks launch", launch);
         }
         check_launch("shared_blocks launch");
     });

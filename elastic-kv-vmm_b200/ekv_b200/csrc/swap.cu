@@ -48,6 +48,8 @@ swap_select_kernel(const __grid_constant__ SelectParams p) {
     __shared__ uint32_t referenced[kMaxHot / 32];
     __shared__ int warp_totals[kSelectWarps];
     __shared__ int found_total;
+    grid_dependency_wait();
+    allow_dependents();
     const unsigned lane = lane_id();
     const int warp = threadIdx.x >> 5;
     const int words = static_cast<int>((p.hot + 31) / 32);
@@ -180,6 +182,8 @@ __device__ __forceinline__ void warp_move(const char* src, char* dst, int64_t by
 // hit.
 __global__ void __launch_bounds__(kPromoteThreads)
 promote_kernel(const __grid_constant__ PromoteParams p) {
+    grid_dependency_wait();
+    allow_dependents();
     const int64_t warps = static_cast<int64_t>(gridDim.x) * kPromoteWarps;
     const int64_t w = static_cast<int64_t>(blockIdx.x) * kPromoteWarps + (threadIdx.x >> 5);
     const unsigned lane = lane_id();
@@ -250,7 +254,8 @@ extern "C" int ekv_swap_select(
         p.promo_row = promo_row_stride;
         p.batch = batch;
         const unsigned grid = static_cast<unsigned>(batch < (1 << 20) ? batch : (1 << 20));
-        swap_select_kernel<<<grid, kSelectThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        launch_dependent(swap_select_kernel, dim3(grid), dim3(kSelectThreads), 0, static_cast<cudaStream_t>(stream),
+                         "swap_select launch", p);
         check_launch("swap_select launch");
     });
 }
@@ -302,7 +307,8 @@ extern "C" int ekv_promote_rows(
         }
         p.addr_or = addr_or;
         const int grid = sm_count(device) * kPromoteBlocksPerSm;
-        promote_kernel<<<grid, kPromoteThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+        launch_dependent(promote_kernel, dim3(grid), dim3(kPromoteThreads), 0, static_cast<cudaStream_t>(stream),
+                         "promote_rows launch", p);
         check_launch("promote_rows launch");
     });
 }

@@ -1,7 +1,7 @@
-// Compiled Python binding of the per-call residency lookups (optional).
+// Compiled Python binding of the per-call residency lookups and gathers (optional).
 //
-// resolve_resident, lookup_slots and the batched shared-prefix resolver are
-// called once per layer per decode step
+// resolve_resident, lookup_slots, the batched shared-prefix resolver and
+// gather_rows / gather_rows_planes are called once per layer per decode step
 // through the reference's Python API.  Through ctypes a call costs ~10 us of
 // host time (reading ~30 tensor attributes in Python and marshalling ~28
 // arguments); here the tensors arrive as at::Tensor and their pointers,
@@ -16,6 +16,7 @@
 #include <torch/extension.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <limits>
 #include <optional>
@@ -31,11 +32,15 @@ constexpr int kKernelError = -1;
 decltype(&ekv_resolve_resident) g_resolve = nullptr;
 decltype(&ekv_lookup_slots) g_lookup = nullptr;
 decltype(&ekv_resolve_shared_blocks) g_shared = nullptr;
+decltype(&ekv_gather_rows) g_gather = nullptr;
+decltype(&ekv_gather_rows_planes) g_gather_planes = nullptr;
 
-void bind(int64_t resolve, int64_t lookup, int64_t shared) {
+void bind(int64_t resolve, int64_t lookup, int64_t shared, int64_t gather, int64_t gather_planes) {
     g_resolve = reinterpret_cast<decltype(&ekv_resolve_resident)>(resolve);
     g_lookup = reinterpret_cast<decltype(&ekv_lookup_slots)>(lookup);
     g_shared = reinterpret_cast<decltype(&ekv_resolve_shared_blocks)>(shared);
+    g_gather = reinterpret_cast<decltype(&ekv_gather_rows)>(gather);
+    g_gather_planes = reinterpret_cast<decltype(&ekv_gather_rows_planes)>(gather_planes);
 }
 
 int index_size(const at::Tensor& t) {
@@ -205,6 +210,118 @@ py::tuple shared_blocks(const at::Tensor& block_ids, const py::sequence& source_
     return py::make_tuple(rc == 0 ? 0 : kKernelError, valid, physical);
 }
 
+// Index tensors of a gather: positions [B, S], request_ids / lengths [B], and the
+// table / slot offsets the addressing mode uses (mode 0 direct, 1 indirect, 2
+// mapped).  Every given tensor CUDA on one device and contiguous (the Python
+// API checks the unused table too); element sizes of the used ones in `es`.
+struct GatherIndex {
+    int device = -1;
+    int es[5] = {0, 0, 0, 8, 8};  // positions, request_ids, lengths, table, offsets
+    const void* table = nullptr;
+    const void* offsets = nullptr;
+};
+
+bool gather_index(const at::Tensor& positions, const at::Tensor& request_ids, const at::Tensor& lengths,
+                  const std::optional<at::Tensor>& request_table, const std::optional<at::Tensor>& slot_offsets,
+                  int mode, GatherIndex& out) {
+    const at::Tensor* table = request_table ? &*request_table : nullptr;
+    const at::Tensor* offsets = slot_offsets ? &*slot_offsets : nullptr;
+    out.device = common_device({&positions, &request_ids, &lengths, table, offsets});
+    if (out.device < 0) return false;
+    for (const at::Tensor* t : {&positions, &request_ids, &lengths, table, offsets}) {
+        if (t && !t->is_contiguous()) return false;
+    }
+    if ((mode >= 1 && !table) || (mode == 1 && !offsets)) return false;
+    out.es[0] = index_size(positions);
+    out.es[1] = index_size(request_ids);
+    out.es[2] = index_size(lengths);
+    if (mode >= 1) {
+        out.es[3] = index_size(*table);
+        out.table = table->data_ptr();
+    }
+    if (mode == 1) {
+        out.es[4] = index_size(*offsets);
+        out.offsets = offsets->data_ptr();
+    }
+    for (int e : out.es) {
+        if (!e) return false;
+    }
+    return true;
+}
+
+bool rows_shape(const at::Tensor& t, int64_t batch, int64_t selected, int64_t width) {
+    return t.dim() == 3 && t.size(0) == batch && t.size(1) == selected && t.size(2) == width;
+}
+
+// gather_rows (the reference's single-plane call).
+int gather_rows(const at::Tensor& raw, const at::Tensor& positions, const at::Tensor& request_ids,
+                const at::Tensor& lengths, const std::optional<at::Tensor>& request_table,
+                const std::optional<at::Tensor>& slot_offsets, const at::Tensor& output, int64_t width,
+                int64_t table_width, int64_t request_stride, int64_t sink_elements, bool indirect) {
+    if (!g_gather || positions.dim() != 2) return kNotHandled;
+    const int64_t batch = positions.size(0), selected = positions.size(1);
+    if (!rows_shape(output, batch, selected, width)) return kNotHandled;
+    if (batch == 0 || selected == 0) return 0;  // no-op, as the reference
+    const int mode = indirect ? 1 : 0;
+    GatherIndex ix;
+    if (!gather_index(positions, request_ids, lengths, request_table, slot_offsets, mode, ix)) return kNotHandled;
+    if (common_device({&raw, &output}) != ix.device || !raw.is_contiguous() || !output.is_contiguous() ||
+        raw.scalar_type() != output.scalar_type()) {
+        return kNotHandled;
+    }
+    const int rc = g_gather(
+        raw.data_ptr(), output.data_ptr(), raw.element_size(), positions.data_ptr(), ix.es[0],
+        request_ids.data_ptr(), ix.es[1], lengths.data_ptr(), ix.es[2], ix.table, ix.es[3], ix.offsets, ix.es[4],
+        batch, selected, width, table_width, request_stride, sink_elements, mode, ix.device, stream_of(ix.device));
+    return rc == 0 ? 0 : kKernelError;
+}
+
+// gather_rows_planes: one row selection over every plane, EKV_MAX_PLANES planes per launch.
+int gather_rows_planes(const std::vector<at::Tensor>& planes, const std::vector<at::Tensor>& outputs,
+                       const at::Tensor& positions, const at::Tensor& request_ids, const at::Tensor& lengths,
+                       const std::optional<at::Tensor>& request_table,
+                       const std::optional<at::Tensor>& slot_offsets, int64_t width, int64_t max_tokens,
+                       int64_t request_stride, int64_t sink_elements, bool indirect, bool mapped) {
+    if (!g_gather_planes || planes.size() != outputs.size() || positions.dim() != 2 || (indirect && mapped)) {
+        return kNotHandled;
+    }
+    const int64_t batch = positions.size(0), selected = positions.size(1);
+    for (const at::Tensor& out : outputs) {
+        if (!rows_shape(out, batch, selected, width)) return kNotHandled;
+    }
+    if (planes.empty() || batch == 0 || selected == 0) return 0;
+    const int mode = mapped ? 2 : (indirect ? 1 : 0);
+    GatherIndex ix;
+    if (!gather_index(positions, request_ids, lengths, request_table, slot_offsets, mode, ix)) return kNotHandled;
+    const at::ScalarType dtype = planes[0].scalar_type();
+    for (size_t p = 0; p < planes.size(); ++p) {
+        const at::Tensor& src = planes[p];
+        const at::Tensor& dst = outputs[p];
+        if (common_device({&src, &dst}) != ix.device || !src.is_contiguous() || !dst.is_contiguous() ||
+            src.scalar_type() != dtype || dst.scalar_type() != dtype) {
+            return kNotHandled;
+        }
+    }
+    // A residency map is indexed by token: its row width is the map's, not the layout's.
+    const int64_t table_width = mode == 2 ? request_table->size(-1) : max_tokens;
+    const int64_t itemsize = planes[0].element_size();
+    void* stream = stream_of(ix.device);
+    uint64_t src[EKV_MAX_PLANES], dst[EKV_MAX_PLANES];
+    for (size_t start = 0; start < planes.size(); start += EKV_MAX_PLANES) {
+        const int n = static_cast<int>(std::min<size_t>(EKV_MAX_PLANES, planes.size() - start));
+        for (int p = 0; p < n; ++p) {
+            src[p] = reinterpret_cast<uint64_t>(planes[start + p].data_ptr());
+            dst[p] = reinterpret_cast<uint64_t>(outputs[start + p].data_ptr());
+        }
+        const int rc = g_gather_planes(
+            src, dst, n, itemsize, positions.data_ptr(), ix.es[0], request_ids.data_ptr(), ix.es[1],
+            lengths.data_ptr(), ix.es[2], ix.table, ix.es[3], ix.offsets, ix.es[4], batch, selected, width,
+            table_width, request_stride, sink_elements, mode, ix.device, stream);
+        if (rc != 0) return kKernelError;
+    }
+    return 0;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -214,6 +331,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("lookup_slots", &lookup_slots, py::arg("residency_map"), py::arg("topk"), py::arg("lengths"),
           py::arg("slots"), py::arg("miss"), py::arg("miss_list"), py::arg("miss_count"), py::arg("compact"));
     m.def("shared_blocks", &shared_blocks);
+    m.def("gather_rows", &gather_rows);
+    m.def("gather_rows_planes", &gather_rows_planes);
     m.attr("NOT_HANDLED") = kNotHandled;
     m.attr("KERNEL_ERROR") = kKernelError;
 }

@@ -9,7 +9,7 @@ use.
 
 from __future__ import annotations
 
-from ._lib import MAX_PLANES, call, index_esize, require_cuda, stream_handle, u64_array
+from ._lib import MAX_PLANES, call, index_esize, last_error, require_cuda, stream_handle, torch_binding, u64_array
 
 
 def _mode(indirect, mapped):
@@ -55,6 +55,18 @@ def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offset
     ELEMENT offsets into ``raw``.  ``raw`` and ``output`` share a dtype: the
     payload is copied bit for bit.
     """
+    fast = torch_binding()
+    if fast is not None:
+        try:
+            rc = fast.gather_rows(raw, positions, request_ids, lengths, request_table, slot_offsets, output,
+                                  layout.row_elements, layout.max_tokens, layout.request_bytes // layout.itemsize,
+                                  layout.chunk_bytes // layout.itemsize, bool(indirect))
+        except TypeError:  # not tensors: the checked path below reports it
+            rc = fast.NOT_HANDLED
+        if rc == 0:
+            return
+        if rc == fast.KERNEL_ERROR:
+            raise last_error("ekv_gather_rows")
     batch, selected = positions.shape
     if output.shape != (batch, selected, layout.row_elements):
         raise ValueError("output shape does not match positions and row width")
@@ -92,6 +104,19 @@ def gather_rows_planes(planes, positions, request_ids, lengths, request_table, s
     s * width``), and ``s < 0`` reads as a zero row -- a lookup and its gather
     in one launch.
     """
+    fast = torch_binding()
+    if fast is not None:
+        try:
+            rc = fast.gather_rows_planes(planes, outputs, positions, request_ids, lengths, request_table,
+                                         slot_offsets, layout.row_elements, layout.max_tokens,
+                                         layout.request_bytes // layout.itemsize,
+                                         layout.chunk_bytes // layout.itemsize, bool(indirect), bool(mapped))
+        except TypeError:  # not tensors: the checked path below reports it
+            rc = fast.NOT_HANDLED
+        if rc == 0:
+            return
+        if rc == fast.KERNEL_ERROR:
+            raise last_error("ekv_gather_rows_planes")
     planes = list(planes)
     outputs = list(outputs)
     if len(planes) != len(outputs):

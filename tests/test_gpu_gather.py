@@ -301,3 +301,82 @@ def test_layer_pipeline_lookup_then_gather(graph, gather_kernel, cuda_device):
     if graph:
         del replay
 
+
+
+def test_compiled_binding_serves_gathers_like_the_ctypes_path(gather_kernel, cuda_device, monkeypatch):
+    """gather_rows and gather_rows_planes (direct, indirect, mapped; more planes than one
+    launch takes) give the same bytes through the compiled binding as through the checked
+    ctypes path (forced by hiding the binding), and the same errors for malformed calls."""
+    from ekv_b200 import _lib, sparse_read
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    assert _lib.torch_binding() is not None, "lib/_ekv_torch.so was not built"
+    dev = cuda_device
+    gen = torch.Generator().manual_seed(41)
+    batch, tokens, width, selected = 3, 96, 64, 50
+    layout = VirtualKVLayout(batch, tokens, width, itemsize=2, chunk_bytes=1 << 16)
+    n_planes = _lib.MAX_PLANES + 7
+    planes = [torch.randint(-30000, 30000, (layout.capacity_bytes // 2,), generator=gen, dtype=torch.int16)
+              .to(dev).view(torch.bfloat16) for _ in range(n_planes)]
+    positions = torch.randint(-3, tokens + 3, (batch, selected), generator=gen).to(dev)
+    ids = torch.tensor([2, 0, 1], device=dev)
+    lengths = torch.tensor([tokens, tokens // 2, 7], device=dev)
+    slots = layout.capacity_bytes // 2 // width
+    offsets = (torch.randperm(slots, generator=gen)[:tokens * batch] * width).to(dev)
+    table = torch.arange(tokens * batch, device=dev).view(batch, tokens)
+    res_map = torch.randint(-1, tokens + 4, (batch, tokens), generator=gen, dtype=torch.int32).to(dev)
+
+    def run():
+        outs = {}
+        for indirect in (False, True):
+            out = torch.full((batch, selected, width), 3.0, dtype=torch.bfloat16, device=dev)
+            sparse_read.gather_rows(planes[0], positions, ids, lengths, table, offsets, out, layout,
+                                    indirect=indirect)
+            outs[("rows", indirect)] = out
+        for mode in ("direct", "indirect", "mapped"):
+            many = [torch.full((batch, selected, width), 3.0, dtype=torch.bfloat16, device=dev)
+                    for _ in range(n_planes)]
+            sparse_read.gather_rows_planes(planes, positions, ids, lengths,
+                                           res_map if mode == "mapped" else table, offsets, many, layout,
+                                           indirect=mode == "indirect", mapped=mode == "mapped")
+            outs[("planes", mode)] = many
+        torch.cuda.synchronize()
+        return outs
+
+    def errors():
+        out = torch.empty((batch, selected, width), dtype=torch.bfloat16, device=dev)
+        found = []
+        for call in (
+            lambda: sparse_read.gather_rows(planes[0], positions, ids, lengths, table, offsets, out[:, 1:], layout,
+                                            indirect=True),
+            lambda: sparse_read.gather_rows(planes[0], positions, ids, lengths, None, offsets, out, layout,
+                                            indirect=True),
+            lambda: sparse_read.gather_rows(planes[0].float(), positions, ids, lengths, table, offsets, out,
+                                            layout, indirect=True),
+            lambda: sparse_read.gather_rows_planes(planes[:2], positions, ids, lengths, table, offsets, [out],
+                                                   layout, indirect=True),
+            lambda: sparse_read.gather_rows_planes(planes[:1], positions, ids, lengths, table, offsets, [out],
+                                                   layout, indirect=True, mapped=True),
+            lambda: sparse_read.gather_rows_planes(planes[:1], positions.cpu(), ids, lengths, table, offsets, [out],
+                                                   layout, indirect=True),
+        ):
+            with pytest.raises((ValueError, TypeError)) as info:
+                call()
+            found.append((info.type, str(info.value)))
+        return found
+
+    fast, fast_errors = run(), errors()
+    monkeypatch.setattr(sparse_read, "torch_binding", lambda: None)
+    slow, slow_errors = run(), errors()
+    assert fast_errors == slow_errors
+    for key, value in fast.items():
+        values = value if isinstance(value, list) else [value]
+        others = slow[key] if isinstance(slow[key], list) else [slow[key]]
+        for a, b in zip(values, others):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16)), key
+    # Direct mode against the oracle, so the shared result is also the right one.
+    want = og.gather_rows(planes[0].view(torch.int16).cpu().numpy(), positions.cpu().numpy(), ids.cpu().numpy(),
+                          lengths.cpu().numpy(), None, None, width=width, table_width=tokens,
+                          request_stride=layout.request_bytes // 2, sink_elements=layout.chunk_bytes // 2,
+                          indirect=False)
+    np.testing.assert_array_equal(fast[("rows", False)].view(torch.int16).cpu().numpy(), want)

@@ -66,8 +66,9 @@ def test_entry_points_validate_before_touching_a_device(library_path):
 
 
 def test_compiled_binding_loads_and_declines_cpu_tensors(library_path):
-    """lib/_ekv_torch.so (built with the library) loads without a GPU; for CPU tensors it
-    reports NOT_HANDLED, so the Python API's checks run and raise its own errors."""
+    """lib/_ekv_torch.so (built with the library) loads without a GPU; for CPU tensors (and
+    malformed calls) it reports NOT_HANDLED, so the Python API's checks run and raise its
+    own errors."""
     import torch
 
     from ekv_b200 import _lib
@@ -87,3 +88,26 @@ def test_compiled_binding_loads_and_declines_cpu_tensors(library_path):
         resolve_resident(*args)
     with pytest.raises(ValueError, match="CUDA tensor"):
         lookup_slots(torch.zeros((2, 8), dtype=torch.int32), torch.zeros((2, 4), dtype=torch.int32))
+
+    from ekv_b200.sparse_read import gather_rows, gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    layout = VirtualKVLayout(2, 8, 4)
+    raw = torch.zeros(layout.capacity_bytes // 2, dtype=torch.bfloat16)
+    pos, ids, lens = torch.zeros((2, 3), dtype=torch.int64), torch.arange(2), torch.full((2,), 8)
+    out = torch.zeros((2, 3, 4), dtype=torch.bfloat16)
+    assert binding.gather_rows(raw, pos, ids, lens, None, None, out, 4, 8, 32, 0, False) == binding.NOT_HANDLED
+    assert binding.gather_rows_planes([raw], [out], pos, ids, lens, None, None, 4, 8, 32, 0, False,
+                                      False) == binding.NOT_HANDLED
+    # A wrong output shape is declined before any device check; the checked path names it.
+    assert binding.gather_rows(raw, pos, ids, lens, None, None, out[:, :2], 4, 8, 32, 0,
+                               False) == binding.NOT_HANDLED
+    with pytest.raises(ValueError, match="output shape"):
+        gather_rows(raw, pos, ids, lens, None, None, out[:, :2], layout, indirect=False)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        gather_rows(raw, pos, ids, lens, None, None, out, layout, indirect=False)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        gather_rows_planes([raw], pos, ids, lens, None, None, [out], layout, indirect=False)
+    # Empty selections are no-ops on both paths.
+    empty = torch.zeros((2, 0), dtype=torch.int64)
+    assert binding.gather_rows(raw, empty, ids, lens, None, None, out[:, :0], 4, 8, 32, 0, False) == 0
