@@ -1086,9 +1086,11 @@ def run_config4(args, dist: Dist):
     hot-slot lookup (R2) of that layer's Top-K followed by the gather of the hits from
     the layer's fixed-position hot pool (direct addressing, misses read as zero rows);
     then the freeable-bitmap AND-combine across ranks.  The 96 launches of a step are
-    replayed from one CUDA graph in plain layer order (the reported value); the same
-    launches with layer i's gather overlapping layer i+1's lookup (``LayerPipeline``)
-    are timed beside it."""
+    replayed from one CUDA graph.  Reported: each layer's lookup and its mapped gather
+    (the gather reads slots from the residency map, not from the lookup) on two
+    streams, forked and joined per layer; timed beside it: the plain layer order
+    (lookup, then the direct gather of its slots) and the pipelined order (layer i's
+    gather beside layer i+1's lookup, which needs every Top-K up front)."""
     import numpy as np
 
     from ekv_b200.resident_lookup import LookupPlan
@@ -1135,17 +1137,25 @@ def run_config4(args, dist: Dist):
 
     from ekv_b200.pipeline import LayerPipeline
 
-    pipeline = LayerPipeline(lookups, gathers, dev)
+    # Mapped gathers read each token's slot from the residency map themselves, so they
+    # need none of the lookup's output and run beside it (slots and miss list are still
+    # produced for the swap-in); same rows as the direct gather of the lookup's slots.
+    ctx_lengths = torch.full((reqs,), ctx, dtype=torch.int64, device=dev)
+    mapped = [PlaneGather(planes[2 * layer:2 * layer + 2], topks[layer], req_ids, ctx_lengths, maps[layer], None,
+                          [out_k, out_v], layout, indirect=False, mapped=True) for layer in range(layers)]
+    pipelines = {"concurrent": LayerPipeline(lookups, mapped, dev, wait=False),
+                 "pipelined": LayerPipeline(lookups, gathers, dev)}
+    modes = ("order", "concurrent", "pipelined")
 
-    def layers_step(overlap=True):
-        if overlap:  # layer i's gather on a second stream while layer i+1's lookup runs
-            pipeline()
+    def layers_step(mode="order"):
+        if mode in pipelines:
+            pipelines[mode]()
             return
         for layer in range(layers):
             lookups[layer]()
             gathers[layer]()
 
-    layers_step(False)
+    layers_step()
     torch.cuda.synchronize()
     # Parity on layer 0 (and the last layer) against the oracle, on this rank's head shard.
     parity = True
@@ -1162,28 +1172,32 @@ def run_config4(args, dist: Dist):
                                   table_width=hot, request_stride=layout.request_bytes // 2,
                                   sink_elements=CHUNK // 2, indirect=False)
             parity &= np.array_equal(out.view(torch.int16).cpu().numpy(), want)
-    # The pipelined step leaves the last layer's rows in the outputs, as the plain one.
-    layers_step(False)
+    # Every form of the step leaves the last layer's rows and lookup outputs of the plain one.
+    layers_step()
     torch.cuda.synchronize()
     plain_out = (out_k.clone(), out_v.clone())
-    out_k.zero_()
-    out_v.zero_()
-    layers_step(True)
-    torch.cuda.synchronize()
-    parity &= bool(torch.equal(out_k, plain_out[0]) and torch.equal(out_v, plain_out[1]))
-    del plain_out
+    plain_lookup = [t.clone() for t in (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count)]
+    for mode in modes[1:]:
+        for t in (out_k, out_v, lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count):
+            t.zero_()
+        layers_step(mode)
+        torch.cuda.synchronize()
+        parity &= bool(torch.equal(out_k, plain_out[0]) and torch.equal(out_v, plain_out[1]))
+        parity &= all(torch.equal(a, b) for a, b in zip(
+            (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count), plain_lookup))
+    del plain_out, plain_lookup
     graphs = {}
     try:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
-            layers_step(True)
-            layers_step(False)
+            for mode in modes:
+                layers_step(mode)
         torch.cuda.current_stream(dev).wait_stream(side)
-        for overlap in (True, False):
-            graphs[overlap] = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graphs[overlap]):
-                layers_step(overlap)
+        for mode in modes:
+            graphs[mode] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graphs[mode]):
+                layers_step(mode)
     except Exception as exc:  # capture unsupported: time eager launches instead
         graphs = {}
         capture_error = str(exc)
@@ -1195,18 +1209,18 @@ def run_config4(args, dist: Dist):
 
     local = torch.zeros(64, dtype=torch.int64, device=dev)
 
-    def step(overlap):
+    def step(mode):
         if graphs:
-            graphs[overlap].replay()
+            graphs[mode].replay()
         else:
-            layers_step(overlap)
+            layers_step(mode)
         combine_freeable(local)
 
+    mode_ms = {}
     with ClockSampler(dist.local_rank) as clocks:
-        ms = timed(lambda: step(False), args.steps, args.warmup, dist)
-        pipelined_ms = timed(lambda: step(True), args.steps, args.warmup, dist)
-    ms_per_step = ms / args.steps
-    pipelined_ms_per_step = pipelined_ms / args.steps
+        for mode in modes:
+            mode_ms[mode] = timed(lambda: step(mode), args.steps, args.warmup, dist) / args.steps
+    ms_per_step = mode_ms["concurrent"]
     units = reqs * k * layers
     hits = reqs * n_hits * layers
     bytes_per_step = hits * 4 * row_bytes + units * (4 + 4 + 4 + 1)  # payload + lookup traffic
@@ -1222,12 +1236,17 @@ def run_config4(args, dist: Dist):
                                f"heads {heads}/rank, bitmap AND-combine per step",
                    "parallelism": f"tp{dist.world} (KV-head sharding; lookup replicated; NCCL AND-combine)",
                    "cuda_graph": bool(graphs), "capture_error": capture_error},
-        "pipelined": {"ms_per_step": pipelined_ms_per_step, "value": units / (pipelined_ms_per_step / 1e3),
-                      "speedup": ms_per_step / pipelined_ms_per_step,
-                      "what": "LayerPipeline: layer i's gather on a second stream while layer i+1's lookup "
-                              "runs; valid only when every layer's Top-K is known when the step starts "
-                              "(a per-layer indexer makes layer i+1's Top-K depend on layer i), so the "
-                              "reported value is the plain layer order"},
+        "step_forms": {
+            "reported": "concurrent: per layer, the lookup (slots, miss mask, miss list) on one stream and the "
+                        "mapped K,V gather (slot read from the residency map) on a second, forked and joined "
+                        "per layer (LayerPipeline wait=False), so it holds when layer i's Top-K is known only "
+                        "after layer i-1",
+            "layer_order": {"ms_per_step": mode_ms["order"], "value": units / (mode_ms["order"] / 1e3),
+                            "what": "lookup, then the direct gather of its slots, layer after layer (the "
+                                    "reference's order)"},
+            "pipelined": {"ms_per_step": mode_ms["pipelined"], "value": units / (mode_ms["pipelined"] / 1e3),
+                          "what": "layer i's direct gather on a second stream while layer i+1's lookup runs; "
+                                  "valid only when every layer's Top-K is known when the step starts"}},
         "hbm_gbs_per_gpu": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_source,

@@ -14,6 +14,15 @@ between them; the caller's stream waits for the last consumer before the call
 returns.  Consumers stay ordered among themselves, so the layers may share one
 output buffer.  It works eagerly and under CUDA graph capture (the second
 stream forks from and joins the caller's stream).
+
+With ``wait=False`` a consumer does not wait for its producer: every layer
+forks (the consumer sees everything issued before the layer) and joins (the
+next layer sees the consumer), so only producer i and consumer i overlap.  That
+is for a consumer that reads none of its producer's output -- the mapped
+gather resolves each token's hot slot from the residency map itself, so layer
+i's lookup (whose slots and miss list feed the swap-in) and layer i's gather
+run at the same time, and it stays valid when layer i's Top-K is only known
+once layer i-1 is done.
 """
 
 from __future__ import annotations
@@ -27,24 +36,34 @@ Launch = Callable[[int], None]
 
 class LayerPipeline:
     """``produce[i](stream)`` then ``consume[i](stream)`` for every layer, with
-    consumer i overlapping producer i+1 (see module docstring)."""
+    consumer i overlapping producer i+1, or with ``wait=False`` producer i alone
+    (see module docstring)."""
 
-    def __init__(self, produce: Sequence[Launch], consume: Sequence[Launch], device):
+    def __init__(self, produce: Sequence[Launch], consume: Sequence[Launch], device, *, wait: bool = True):
         self.produce, self.consume = list(produce), list(consume)
         if not self.produce or len(self.produce) != len(self.consume):
             raise ValueError("need one producer and one consumer per layer, at least one layer")
         self.device = torch.device(device)
+        self.wait = bool(wait)
         self.side = torch.cuda.Stream(self.device)
         self.ready = [torch.cuda.Event() for _ in self.produce]
+        self.done = [torch.cuda.Event() for _ in self.produce]
 
     def __call__(self) -> None:
         main = torch.cuda.current_stream(self.device)
         side = self.side
         side.wait_stream(main)  # fork: the consumers see everything issued before the step
         main_handle, side_handle = main.cuda_stream, side.cuda_stream
-        for produce, consume, ready in zip(self.produce, self.consume, self.ready):
+        for produce, consume, ready, done in zip(self.produce, self.consume, self.ready, self.done):
+            if not self.wait:  # fork: consumer i sees everything before layer i, not producer i
+                ready.record(main)
+                side.wait_event(ready)
             produce(main_handle)
-            ready.record(main)
-            side.wait_event(ready)
+            if self.wait:
+                ready.record(main)
+                side.wait_event(ready)
             consume(side_handle)
+            if not self.wait:  # join: layer i+1 sees consumer i
+                done.record(side)
+                main.wait_event(done)
         main.wait_stream(side)  # join

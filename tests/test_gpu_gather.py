@@ -234,11 +234,14 @@ def test_mapped_gather_reads_slots_outside_the_region_as_absent(gather_kernel, c
 
 
 @pytest.mark.parametrize("graph", [False, True])
-def test_layer_pipeline_lookup_then_gather(graph, gather_kernel, cuda_device):
-    """LayerPipeline over per-layer (lookup, direct gather) pairs -- the config-4 decode
-    step with layer i's gather overlapping layer i+1's lookup -- gives every layer's
-    rows exactly as the oracle's lookup + gather; with ``graph`` it is captured once
-    and replayed."""
+@pytest.mark.parametrize("form", ["pipelined", "concurrent"])
+def test_layer_pipeline_lookup_then_gather(form, graph, gather_kernel, cuda_device):
+    """LayerPipeline over per-layer (lookup, gather) pairs -- the config-4 decode step --
+    gives every layer's slots and rows exactly as the oracle's lookup + gather.
+    ``pipelined``: direct gathers of the lookup's slots, layer i's gather beside layer
+    i+1's lookup.  ``concurrent`` (wait=False): mapped gathers that read the residency
+    map themselves, beside their own layer's lookup.  With ``graph`` the step is
+    captured once and replayed."""
     from ekv_b200.pipeline import LayerPipeline
     from ekv_b200.resident_lookup import LookupPlan
     from ekv_b200.sparse_read import PlaneGather
@@ -251,6 +254,7 @@ def test_layer_pipeline_lookup_then_gather(graph, gather_kernel, cuda_device):
     layout = VirtualKVLayout(batch, hot, width, itemsize=2, chunk_bytes=1 << 16)
     req_ids = torch.arange(batch, device=dev)
     lengths = torch.full((batch,), hot, dtype=torch.int64, device=dev)
+    ctx_lengths = torch.full((batch,), context, dtype=torch.int64, device=dev)
     maps, topks, planes, outs, lookups, gathers = [], [], [], [], [], []
     for _ in range(layers):
         res_map = torch.full((batch, context), -1, dtype=torch.int32)
@@ -266,12 +270,27 @@ def test_layer_pipeline_lookup_then_gather(graph, gather_kernel, cuda_device):
         planes.append(layer_planes)
         layer_outs = [torch.full((batch, k, width), 7, dtype=torch.int16, device=dev) for _ in range(2)]
         outs.append(layer_outs)
-        plan = LookupPlan(res_map.to(dev), topk.to(dev))
+        dmap, dtopk = res_map.to(dev), topk.to(dev)
+        plan = LookupPlan(dmap, dtopk)
         lookups.append(plan)
-        gathers.append(PlaneGather([p.to(dev).view(torch.bfloat16) for p in layer_planes], plan.slots, req_ids,
-                                   lengths, None, None, [o.view(torch.bfloat16) for o in layer_outs], layout,
-                                   indirect=False))
-    pipeline = LayerPipeline(lookups, gathers, dev)
+        dev_planes = [p.to(dev).view(torch.bfloat16) for p in layer_planes]
+        if form == "pipelined":
+            gathers.append(PlaneGather(dev_planes, plan.slots, req_ids, lengths, None, None,
+                                       [o.view(torch.bfloat16) for o in layer_outs], layout, indirect=False))
+        else:
+            gathers.append(PlaneGather(dev_planes, dtopk, req_ids, ctx_lengths, dmap, None,
+                                       [o.view(torch.bfloat16) for o in layer_outs], layout, indirect=False,
+                                       mapped=True))
+    pipeline = LayerPipeline(lookups, gathers, dev, wait=form == "pipelined")
+
+    def poison():  # the plans ran their lookup once when built: make the step's own run visible
+        for plan in lookups:
+            for t in (plan.slots, plan.miss_list, plan.miss_count):
+                t.fill_(-5)
+        for layer_outs in outs:
+            for o in layer_outs:
+                o.fill_(7)
+
     if graph:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
@@ -279,19 +298,20 @@ def test_layer_pipeline_lookup_then_gather(graph, gather_kernel, cuda_device):
             pipeline()
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize()
-        for layer_outs in outs:
-            for o in layer_outs:
-                o.fill_(7)
         replay = torch.cuda.CUDAGraph()
         with torch.cuda.graph(replay):
             pipeline()
+        poison()
         replay.replay()
     else:
+        poison()
         pipeline()
     torch.cuda.synchronize()
     for layer in range(layers):
-        slots, _, _, _ = ol.lookup_slots(maps[layer].numpy(), topks[layer].numpy())
+        slots, _, miss_list, miss_count = ol.lookup_slots(maps[layer].numpy(), topks[layer].numpy())
         np.testing.assert_array_equal(lookups[layer].slots.cpu().numpy(), slots)
+        np.testing.assert_array_equal(lookups[layer].miss_list.cpu().numpy(), miss_list)
+        np.testing.assert_array_equal(lookups[layer].miss_count.cpu().numpy(), miss_count)
         want = og.gather_rows_planes([p.numpy() for p in planes[layer]], slots, req_ids.cpu().numpy(),
                                      lengths.cpu().numpy(), None, None, width=width, table_width=hot,
                                      request_stride=layout.request_bytes // 2,
