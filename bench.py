@@ -1003,6 +1003,7 @@ def bitmap_bench(dist: Dist, reps: int = 50, shard: int = 0):
 # --------------------------------------------------------------------------- arms
 
 def run_ours(args, dist: Dist):
+    from ekv_b200._lib import torch_binding
     from ekv_b200.sparse_read import gather_rows_planes
 
     work = Workload(dist, args.layers or CFG2["layers"], args.tp_shard)
@@ -1060,7 +1061,9 @@ def run_ours(args, dist: Dist):
                          "h2d_bytes_per_step": pos_host.numel() * pos_host.element_size(),
                          "d2h_bytes_per_step": result_host.numel() * result_host.element_size(),
                          "steps": e2e_steps, "ms_per_step": ms_e2e / e2e_steps,
-                         "api": "ekv_b200.sparse_read.gather_rows_planes (ctypes -> ekv_gather_rows_planes)"}
+                         "api": "ekv_b200.sparse_read.gather_rows_planes ("
+                                + ("compiled binding" if torch_binding() is not None else "ctypes")
+                                + " -> ekv_gather_rows_planes)"}
         result["gpu_launches"] = args.steps  # the e2e loop is timed separately
 
     result["bitmap"] = bitmap_bench(dist)
