@@ -1240,10 +1240,11 @@ def run_config4(args, dist: Dist):
                    "parallelism": f"tp{dist.world} (KV-head sharding; lookup replicated; NCCL AND-combine)",
                    "cuda_graph": bool(graphs), "capture_error": capture_error},
         "step_forms": {
-            "reported": "concurrent: per layer, the lookup (slots, miss mask, miss list) on one stream and the "
-                        "mapped K,V gather (slot read from the residency map) on a second, forked and joined "
-                        "per layer (LayerPipeline wait=False), so it holds when layer i's Top-K is known only "
-                        "after layer i-1",
+            "reported": "concurrent: the mapped K,V gathers (slot read from the residency map) back to back "
+                        "on the step's stream, each layer's lookup (slots, miss mask, miss list) forked onto a "
+                        "second stream at the start of its layer and joined at the end of the step "
+                        "(LayerPipeline wait=False), so it holds when layer i's Top-K is known only after "
+                        "layer i-1",
             "layer_order": {"ms_per_step": mode_ms["order"], "value": units / (mode_ms["order"] / 1e3),
                             "what": "lookup, then the direct gather of its slots, layer after layer (the "
                                     "reference's order)"},

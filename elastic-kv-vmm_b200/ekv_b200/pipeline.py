@@ -15,14 +15,16 @@ returns.  Consumers stay ordered among themselves, so the layers may share one
 output buffer.  It works eagerly and under CUDA graph capture (the second
 stream forks from and joins the caller's stream).
 
-With ``wait=False`` a consumer does not wait for its producer: every layer
-forks (the consumer sees everything issued before the layer) and joins (the
-next layer sees the consumer), so only producer i and consumer i overlap.  That
-is for a consumer that reads none of its producer's output -- the mapped
-gather resolves each token's hot slot from the residency map itself, so layer
-i's lookup (whose slots and miss list feed the swap-in) and layer i's gather
-run at the same time, and it stays valid when layer i's Top-K is only known
-once layer i-1 is done.
+With ``wait=False`` a consumer does not wait for its producer.  That is for a
+consumer that reads none of its producer's output -- the mapped gather resolves
+each token's hot slot from the residency map itself, so layer i's lookup (whose
+slots and miss list feed the swap-in) and layer i's gather can run at the same
+time.  Then the consumers run back to back on the caller's stream (where
+programmatic dependent launch chains them) and each producer is forked onto the
+second stream at the start of its layer (it sees everything issued before
+layer i, e.g. the work that produced layer i's Top-K, but not consumer i); the
+caller's stream joins the second stream once, at the end.  It stays valid when
+layer i's Top-K is only known once layer i-1 is done.
 """
 
 from __future__ import annotations
@@ -47,23 +49,22 @@ class LayerPipeline:
         self.wait = bool(wait)
         self.side = torch.cuda.Stream(self.device)
         self.ready = [torch.cuda.Event() for _ in self.produce]
-        self.done = [torch.cuda.Event() for _ in self.produce]
 
     def __call__(self) -> None:
         main = torch.cuda.current_stream(self.device)
         side = self.side
-        side.wait_stream(main)  # fork: the consumers see everything issued before the step
+        side.wait_stream(main)  # fork: the second stream sees everything issued before the step
         main_handle, side_handle = main.cuda_stream, side.cuda_stream
-        for produce, consume, ready, done in zip(self.produce, self.consume, self.ready, self.done):
-            if not self.wait:  # fork: consumer i sees everything before layer i, not producer i
+        if self.wait:
+            for produce, consume, ready in zip(self.produce, self.consume, self.ready):
+                produce(main_handle)
                 ready.record(main)
                 side.wait_event(ready)
-            produce(main_handle)
-            if self.wait:
-                ready.record(main)
+                consume(side_handle)
+        else:
+            for produce, consume, ready in zip(self.produce, self.consume, self.ready):
+                ready.record(main)  # fork producer i off everything before layer i
                 side.wait_event(ready)
-            consume(side_handle)
-            if not self.wait:  # join: layer i+1 sees consumer i
-                done.record(side)
-                main.wait_event(done)
+                produce(side_handle)
+                consume(main_handle)
         main.wait_stream(side)  # join
