@@ -41,6 +41,28 @@ def test_counts_and_bitmap_match_reference(index, cuda_device):
     assert int(projection.overflow.item()) == 0
 
 
+@pytest.mark.parametrize("owners", [2, 3])
+def test_shared_chunk_is_freeable_only_with_every_owner(owners, cuda_device):
+    """tests/test_scheduler_budget.py:414-426 and :769-775 on the device: a chunk owned by
+    ``owners`` pages is in the freeable bitmap only for a candidate set holding all of them."""
+    import itertools
+
+    from ekv_b200.releasable import ChunkProjection, bitmap_to_chunks, chunks_to_bitmap, freeable_bitmap
+
+    planes, page_size, chunk_bytes, n = [(9, 16)], 4, 256, 64  # pages 0-3 all lie in chunk 9
+    projection = ChunkProjection(planes, page_size, chunk_bytes, n, cuda_device)
+    refs = torch.zeros(n, dtype=torch.int32, device=cuda_device)
+    refs[9] = owners
+    pages = list(range(1, owners + 1))
+    for mapped_chunks in ({9}, set()):
+        mapped = chunks_to_bitmap(mapped_chunks, n, cuda_device)
+        for size in range(1, owners + 1):
+            for subset in itertools.combinations(pages, size):
+                counts = projection.counts(torch.tensor(subset, dtype=torch.int64, device=cuda_device))
+                want = {9} if size == owners and mapped_chunks else set()
+                assert bitmap_to_chunks(freeable_bitmap(counts, refs, mapped)) == want
+
+
 def test_plans_fixture_joint_chunks(cuda_device):
     """The captured TP4 state: per-rank bitmaps of the pair [1, 2] AND to the 120 chunks."""
     from ekv_b200.releasable import (ChunkProjection, bitmap_and, bitmap_to_chunks, chunks_to_bitmap,

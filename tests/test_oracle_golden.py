@@ -151,6 +151,35 @@ def test_releasable_oracle_matches_reference(index):
         assert sorted(orl.chunks_of_bits(bits)) == expected
 
 
+SHARED_CHUNK = dict(planes=[(9, 16)], page_size=4, chunk_bytes=256, n_chunks=64)  # pages 0-3 all in chunk 9
+
+
+@pytest.mark.parametrize("owners", [2, 3])
+def test_shared_chunk_is_freeable_only_with_every_owner(owners):
+    """Known answers of tests/test_scheduler_budget.py:414-426 (a chunk with three owning
+    candidates: no two of them free it, all three do) and :769-775 (two owners: neither
+    alone, the pair does), through the set form and the bitmap form the kernels restate."""
+    import itertools
+
+    g = SHARED_CHUNK
+    chunks_of = lambda page: orl.page_chunks(page, g["planes"], g["page_size"], g["chunk_bytes"])  # noqa: E731
+    pages = list(range(1, owners + 1))
+    assert all(chunks_of(p) == {9} for p in pages)
+    refs, mapped = {9: owners}, {9}
+    refs_arr = np.zeros(g["n_chunks"], dtype=np.int32)
+    refs_arr[9] = owners
+    mapped_bits = orl.bits_of(mapped, g["n_chunks"])
+    for size in range(1, owners + 1):
+        for subset in itertools.combinations(pages, size):
+            want = {9} if size == owners else set()
+            assert orl.releasable(chunks_of, refs, mapped, subset) == want
+            assert orl.releasable_group(chunks_of, refs, mapped, [[p] for p in subset]) == want
+            counts = orl.chunk_counts_np(sorted(subset), g["planes"], g["page_size"], g["chunk_bytes"],
+                                         g["n_chunks"])
+            assert orl.chunks_of_bits(orl.freeable_bitmap_np(counts, refs_arr, mapped_bits)) == want
+    assert orl.releasable(chunks_of, refs, set(), pages) == set()  # an unmapped chunk is never freeable
+
+
 def test_plans_fixture_pair_frees_120_chunks_on_every_rank():
     """README.md:30 / results/vmm-pair12k-shadow: neither request alone frees a
     chunk; the pair frees 120 chunks (240 MiB) on each of the 4 TP ranks."""
