@@ -182,9 +182,27 @@ class PeerFreeableCombiner:
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     def combine(self, counts=None, refs=None, mapped_bits=None, *, local_bits=None, out=None, local_out=None):
-        """AND over the ranks of every rank's freeable bitmap; returns ``out`` (int64 words)."""
+        """AND over the ranks of every rank's freeable bitmap; returns ``out`` (int64 words).
+
+        The local bitmap is built from ``counts`` / ``refs`` (int32, n_chunks) and
+        ``mapped_bits`` (int64 words), or taken from ``local_bits`` (int64 words).
+        """
+        if local_bits is None and (counts is None or refs is None or mapped_bits is None):
+            raise ValueError("give counts, refs and mapped_bits, or local_bits")
         if out is None:
             out = torch.empty(self.n_words, dtype=torch.int64, device=self.device)
+        expected = dict(counts=(torch.int32, self.n_chunks), refs=(torch.int32, self.n_chunks),
+                        mapped_bits=(torch.int64, self.n_words), local_bits=(torch.int64, self.n_words),
+                        out=(torch.int64, self.n_words), local_out=(torch.int64, self.n_words))
+        given = dict(counts=counts, refs=refs, mapped_bits=mapped_bits, local_bits=local_bits, out=out,
+                     local_out=local_out)
+        require_cuda(given, self.device)
+        for name, tensor in given.items():
+            if tensor is None:
+                continue
+            dtype, numel = expected[name]
+            if tensor.dtype != dtype or tensor.numel() != numel or not tensor.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous {dtype} tensor of {numel} elements")
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         call("ekv_freeable_and_peers",
              None if counts is None else counts.data_ptr(), None if refs is None else refs.data_ptr(),

@@ -164,6 +164,11 @@ def test_peer_combine_single_rank_equals_freeable_bitmap(cuda_device):
         counts, refs, mapped = _peer_inputs(gen, n, cuda_device)
         assert torch.equal(combiner.combine(counts, refs, mapped), freeable_bitmap(counts, refs, mapped))
     assert not combiner.failed()
+    # Tensors of the wrong size or type are refused before the launch.
+    for bad in (dict(counts=counts[:-1]), dict(refs=refs.long()), dict(mapped_bits=mapped[:-1])):
+        args = dict(counts=counts, refs=refs, mapped_bits=mapped) | bad
+        with pytest.raises(ValueError, match="contiguous"):
+            combiner.combine(**args)
 
 
 def test_peer_combine_two_ranks_with_the_peer_already_arrived(cuda_device):

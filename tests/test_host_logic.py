@@ -567,3 +567,22 @@ def test_layer_pipeline_contract():
         LayerPipeline([], [], "cpu")
     with pytest.raises(ValueError, match="one producer and one consumer"):
         LayerPipeline([lambda s: None], [], "cpu")
+
+
+def test_peer_combiner_checks_its_arguments():
+    """PeerFreeableCombiner.combine refuses a call without a local bitmap source and
+    tensors that are not CUDA tensors of the combiner's sizes, before any launch."""
+    import torch
+
+    from ekv_b200.releasable import PeerFreeableCombiner
+
+    combiner = PeerFreeableCombiner(100, "cpu", buffers=[0x1000], rank=0)
+    assert combiner.n_words == 2
+    with pytest.raises(ValueError, match="counts, refs and mapped_bits, or local_bits"):
+        combiner.combine()
+    with pytest.raises(ValueError, match="counts, refs and mapped_bits, or local_bits"):
+        combiner.combine(torch.zeros(100, dtype=torch.int32), torch.zeros(100, dtype=torch.int32))
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        combiner.combine(local_bits=torch.zeros(2, dtype=torch.int64), out=torch.zeros(2, dtype=torch.int64))
+    with pytest.raises(ValueError, match="rank is required"):
+        PeerFreeableCombiner(100, "cpu", buffers=[0x1000])
