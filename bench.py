@@ -1226,7 +1226,10 @@ def run_config4(args, dist: Dist):
     ms_per_step = mode_ms["concurrent"]
     units = reqs * k * layers
     hits = reqs * n_hits * layers
-    bytes_per_step = hits * 4 * row_bytes + units * (4 + 4 + 4 + 1)  # payload + lookup traffic
+    misses = units - hits
+    # K and V: a hit row is read and written, a miss row written as zeros; lookup: 13 B per
+    # Top-K id (index, map entry, slot, mask) + 4 B per miss-list entry.
+    bytes_per_step = hits * 4 * row_bytes + misses * 2 * row_bytes + units * (4 + 4 + 4 + 1) + misses * 4
     peak, peak_source = measured_hbm_peak()
     achieved = bytes_per_step / (ms_per_step / 1e3) / 1e9
     result = {
@@ -1254,8 +1257,9 @@ def run_config4(args, dist: Dist):
         "hbm_gbs_per_gpu": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_source,
-                     "note": "step = 48 lookups + 48 two-plane gathers; bytes = hit rows x 4 x row_bytes + "
-                             "13 B per lookup"},
+                     "note": "step = 48 lookups + 48 two-plane gathers; bytes = hit rows x 4 x row_bytes "
+                             "(K and V read and written) + miss rows x 2 x row_bytes (zero rows written) + "
+                             "13 B per lookup + 4 B per miss-list entry"},
         "parity_layer0_and_last": bool(parity), "bitmap": bitmap,
         "gpu_launches": 2 * layers * args.steps + args.steps * (dist.world > 1),
         "clocks": clocks.summary(),
