@@ -65,6 +65,24 @@ constexpr int kGatherWarps = kGatherThreads / 32;
 constexpr int kGatherBlocksPerSM = EKV_GATHER_MIN_BLOCKS;
 constexpr int kUnroll = EKV_GATHER_UNROLL;
 
+// Rows of at most EKV_GATHER_SMALL_ROW_BYTES per plane (the 256 B rows of a TP8 head
+// shard) over more planes than the default instance flattens (all layers' K and V
+// in one launch) take a second instance of the kernel: every aligned batch
+// flattened and EKV_GATHER_SMALL_UNROLL vectors in flight per lane.  Measured on
+// B200 (config 2, 36 layers): 0.916 instead of 0.902 of the copy peak at 256 B rows,
+// while at 512 B and 2 KiB rows the same setting was 0.4-0.7 % slower.  A launch
+// over few planes (one layer) keeps the default instance: it already flattens
+// them, and its 86 registers leave room on each SM for a lookup block beside two
+// gather blocks (the small-row instance takes 94).
+#ifndef EKV_GATHER_SMALL_ROW_BYTES
+#define EKV_GATHER_SMALL_ROW_BYTES 256  // 0 turns the small-row instance off
+#endif
+#ifndef EKV_GATHER_SMALL_UNROLL
+#define EKV_GATHER_SMALL_UNROLL 12
+#endif
+constexpr int64_t kSmallRowBytes = EKV_GATHER_SMALL_ROW_BYTES;
+constexpr int kSmallUnroll = EKV_GATHER_SMALL_UNROLL;
+
 // Byte offset of row r inside every source plane, or valid = false.
 __device__ __forceinline__ int64_t resolve_row(const GatherParams& p, int64_t r, bool& valid) {
     const int64_t b = r / p.selected;
@@ -177,17 +195,18 @@ __device__ __forceinline__ void copy_row_any(const GatherParams& p, bool valid, 
 #endif
 constexpr uint32_t kFlatRowLimit = EKV_GATHER_FLAT_LIMIT;  // vectors per row (all planes) up to which to flatten
 
+template <int kU>
 __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t mine, int64_t row0,
                                                  int64_t warps, int nb, unsigned lane) {
     const uint32_t vecs = static_cast<uint32_t>(p.row_bytes >> 4);
     const uint32_t per_row = static_cast<uint32_t>(p.n_planes) * vecs;
     const uint32_t total = static_cast<uint32_t>(nb) * per_row;
-    for (uint32_t base = 0; base < total; base += 32 * kUnroll) {
-        uint4 v[kUnroll];
-        uint32_t row_of[kUnroll];
-        uint32_t rem_of[kUnroll];
+    for (uint32_t base = 0; base < total; base += 32 * kU) {
+        uint4 v[kU];
+        uint32_t row_of[kU];
+        uint32_t rem_of[kU];
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < kU; ++u) {
             const uint32_t idx = base + u * 32 + lane;
             const uint32_t k = idx < total ? idx / per_row : 0;
             const int64_t s = __shfl_sync(0xffffffffu, mine, static_cast<int>(k));
@@ -202,7 +221,7 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
             }
         }
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < kU; ++u) {
             const uint32_t idx = base + u * 32 + lane;
             if (idx < total) {
                 const uint32_t plane = p.vec_shift >= 0 ? (rem_of[u] >> p.vec_shift) : rem_of[u] / vecs;
@@ -218,6 +237,11 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
 // resolves one row's index chain, so the three dependent index loads are paid
 // once per 32 rows instead of once per row; the warp then streams each row out
 // of all planes with the offset broadcast from its lane.
+//
+// kU: vectors in flight per lane in the flattened batch copy; kFlatAll: flatten
+// every 16-byte-aligned batch, whatever its row size (the small-row instance,
+// whose rows x planes x vectors stay far below 2^32).
+template <int kU, bool kFlatAll>
 __global__ void __launch_bounds__(kGatherThreads, kGatherBlocksPerSM)
 gather_kernel(const __grid_constant__ GatherParams p) {
     grid_dependency_wait();
@@ -243,9 +267,9 @@ gather_kernel(const __grid_constant__ GatherParams p) {
         const int64_t left = (n_rows - row0 + warps - 1) / warps;
         const int nb = static_cast<int>(left < 32 ? left : 32);
         const bool small_rows = p.row_bytes % 16 == 0 && p.plane_or % 16 == 0 &&
-                                static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) <= kFlatRowLimit;
+                                (kFlatAll || static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) <= kFlatRowLimit);
         if (small_rows && !__ballot_sync(0xffffffffu, valid && (src & 15))) {
-            copy_batch_vec16(p, mine, row0, warps, nb, lane);
+            copy_batch_vec16<kU>(p, mine, row0, warps, nb, lane);
             continue;
         }
         for (int k = 0; k < nb; ++k) {
@@ -428,12 +452,21 @@ bool bulk_allowed() {
     return mode && std::strcmp(mode, "bulk") == 0;
 }
 
-int gather_grid(int device, int64_t n_rows) {
-    static int cached[64] = {0};
-    int grid = device < 64 ? cached[device] : 0;
+using GatherKernel = void (*)(GatherParams);
+
+// The kernel instance for `n_planes` planes of `row_bytes` rows.
+GatherKernel gather_kernel_for(int64_t row_bytes, int n_planes, bool& small) {
+    small = kSmallRowBytes > 0 && row_bytes <= kSmallRowBytes &&
+            static_cast<uint64_t>(n_planes) * (row_bytes >> 4) > kFlatRowLimit;
+    return small ? gather_kernel<kSmallUnroll, true> : gather_kernel<kUnroll, false>;
+}
+
+int gather_grid(GatherKernel kernel, bool small, int device, int64_t n_rows) {
+    static int cached[2][64] = {{0}};
+    int grid = device < 64 ? cached[small][device] : 0;
     if (!grid) {
-        grid = persistent_grid(reinterpret_cast<const void*>(gather_kernel), kGatherThreads, 0, device);
-        if (device < 64) cached[device] = grid;
+        grid = persistent_grid(reinterpret_cast<const void*>(kernel), kGatherThreads, 0, device);
+        if (device < 64) cached[small][device] = grid;
     }
     const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
     return static_cast<int>(needed < grid ? needed : grid);
@@ -520,7 +553,9 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
             const unsigned grid = static_cast<unsigned>(needed < sms ? needed : sms);
             gather_bulk_kernel<<<grid, kBulkThreads, shape.smem, s>>>(p, shape.slots, shape.slot_bytes);
         } else {
-            launch_dependent(gather_kernel, dim3(gather_grid(device, n_rows)), dim3(kGatherThreads), 0, s,
+            bool small = false;
+            const GatherKernel kernel = gather_kernel_for(p.row_bytes, p.n_planes, small);
+            launch_dependent(kernel, dim3(gather_grid(kernel, small, device, n_rows)), dim3(kGatherThreads), 0, s,
                              "gather_rows launch", p);
         }
         check_launch("gather_rows launch");
