@@ -400,3 +400,39 @@ def test_compiled_binding_serves_gathers_like_the_ctypes_path(gather_kernel, cud
                           request_stride=layout.request_bytes // 2, sink_elements=layout.chunk_bytes // 2,
                           indirect=False)
     np.testing.assert_array_equal(fast[("rows", False)].view(torch.int16).cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("indirect", [False, True])
+def test_small_rows_over_many_planes_match_the_oracle(indirect, gather_kernel, cuda_device):
+    """256 B rows over more planes than the default kernel instance flattens (the TP8
+    shard of every layer in one launch) take the small-row instance; its bytes equal the
+    oracle's, invalid positions give zero rows, and a batch holding a row that is not
+    16-byte aligned falls back to element copies."""
+    from ekv_b200.sparse_read import gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    gen = torch.Generator().manual_seed(43)
+    batch, tokens, width, selected, n_planes = 5, 300, 128, 180, 20
+    layout = VirtualKVLayout(batch, tokens, width, itemsize=2, chunk_bytes=1 << 16)
+    elems = layout.capacity_bytes // 2
+    planes = [torch.randint(-30000, 30000, (elems,), generator=gen, dtype=torch.int16) for _ in range(n_planes)]
+    positions = torch.randint(-4, tokens + 4, (batch, selected), generator=gen)
+    ids = torch.tensor([3, 1, 4, 0, 2])
+    lengths = torch.tensor([tokens, 250, 17, tokens, 0])
+    n_logical = batch * tokens
+    table = torch.randperm(n_logical, generator=gen).view(batch, tokens)
+    offsets = layout.chunk_bytes // 2 + torch.randperm(elems // width - layout.chunk_bytes // 2 // width,
+                                                      generator=gen)[:n_logical] * width
+    offsets[table[0, 5]] = layout.chunk_bytes // 2 + 3  # one row not 16-byte aligned (request 0, token 5)
+    positions[3, 0] = 5  # batch row 3 is request 0: the unaligned row is selected
+    outs = [torch.full((batch, selected, width), 9, dtype=torch.int16, device=cuda_device) for _ in planes]
+    gather_rows_planes([p.to(cuda_device).view(torch.bfloat16) for p in planes], positions.to(cuda_device),
+                       ids.to(cuda_device), lengths.to(cuda_device), table.to(cuda_device),
+                       offsets.to(cuda_device), [o.view(torch.bfloat16) for o in outs], layout, indirect=indirect)
+    torch.cuda.synchronize()
+    want = og.gather_rows_planes([p.numpy() for p in planes], positions.numpy(), ids.numpy(), lengths.numpy(),
+                                 table.numpy(), offsets.numpy(), width=width, table_width=tokens,
+                                 request_stride=layout.request_bytes // 2, sink_elements=layout.chunk_bytes // 2,
+                                 indirect=indirect)
+    for out, exp in zip(outs, want):
+        np.testing.assert_array_equal(out.cpu().numpy(), exp)
