@@ -14,6 +14,7 @@
 // when the chunk table fits in shared memory each block accumulates a private
 // histogram there and flushes its non-zero bins once.  The bitmap is built with
 // warp ballots (32 chunks per ballot, two ballots per 64-bit word).
+#include <atomic>
 #include <vector>
 
 #include "common.cuh"
@@ -272,12 +273,12 @@ extern "C" int ekv_chunk_counts(
         // grouped histogram when the chunk table fits in shared memory.
         std::vector<char> grouped(n_planes, 0);
         if (n_chunks < kSharedChunkLimit) {
-            static bool grouped_configured[64] = {false};
-            if (device < 64 && !grouped_configured[device]) {
+            static std::atomic<bool> grouped_configured[64];  // per device; a race configures twice
+            if (device >= 64 || !grouped_configured[device].load(std::memory_order_relaxed)) {
                 cuda_check(cudaFuncSetAttribute(grouped_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(kSharedChunkLimit * sizeof(int32_t))),
                            "configure grouped histogram");
-                grouped_configured[device] = true;
+                if (device < 64) grouped_configured[device].store(true, std::memory_order_relaxed);
             }
             for (int i = 0; i < n_planes; ++i) {
                 if (grouped[i]) continue;
@@ -319,13 +320,13 @@ extern "C" int ekv_chunk_counts(
         const int64_t tasks = n_pages * p.n_planes;
         if (n_chunks <= kSharedChunkLimit) {
             const size_t smem = static_cast<size_t>(n_chunks) * sizeof(int32_t);
-            static bool configured[64] = {false};
-            if (device < 64 && !configured[device]) {
+            static std::atomic<bool> configured[64];  // per device; a race configures twice
+            if (device >= 64 || !configured[device].load(std::memory_order_relaxed)) {
                 cuda_check(cudaFuncSetAttribute(chunk_count_kernel<true>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(kSharedChunkLimit * sizeof(int32_t))),
                            "configure shared histogram");
-                configured[device] = true;
+                if (device < 64) configured[device].store(true, std::memory_order_relaxed);
             }
             // Few blocks: each one pays a full-table flush.
             const int64_t needed = (tasks + kCountThreads - 1) / kCountThreads;

@@ -19,6 +19,7 @@
 // resident blocks.  Rows whose addresses are not 16-byte aligned fall back to
 // the widest element size that divides every address.  A bulk-copy (TMA
 // engine) variant is kept for comparison; see bulk_allowed().
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
@@ -421,12 +422,12 @@ struct BulkShape {
 
 // Ring geometry for rows of `row_bytes`, or slots == 0 when rows are too big.
 BulkShape bulk_shape(int device, int64_t row_bytes) {
-    static int optin[64] = {0};
-    int limit = device < 64 ? optin[device] : 0;
+    static std::atomic<int> optin[64];  // per device; a race queries twice
+    int limit = device < 64 ? optin[device].load(std::memory_order_relaxed) : 0;
     if (!limit) {
         cuda_check(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device),
                    "query shared memory limit");
-        if (device < 64) optin[device] = limit;
+        if (device < 64) optin[device].store(limit, std::memory_order_relaxed);
     }
     BulkShape shape;
     if (row_bytes <= 0 || row_bytes % 16 || row_bytes > (1 << 20)) return shape;
@@ -462,11 +463,11 @@ GatherKernel gather_kernel_for(int64_t row_bytes, int n_planes, bool& small) {
 }
 
 int gather_grid(GatherKernel kernel, bool small, int device, int64_t n_rows) {
-    static int cached[2][64] = {{0}};
-    int grid = device < 64 ? cached[small][device] : 0;
+    static std::atomic<int> cached[2][64];  // per instance and device; a race computes twice
+    int grid = device < 64 ? cached[small][device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
         grid = persistent_grid(reinterpret_cast<const void*>(kernel), kGatherThreads, 0, device);
-        if (device < 64) cached[small][device] = grid;
+        if (device < 64) cached[small][device].store(grid, std::memory_order_relaxed);
     }
     const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
     return static_cast<int>(needed < grid ? needed : grid);
@@ -541,12 +542,12 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         const BulkShape shape = (plane_or % 16 == 0 && bulk_allowed()) ? bulk_shape(device, p.row_bytes)
                                                                         : BulkShape{};
         if (shape.slots) {
-            static size_t configured[64] = {0};
-            if (device >= 64 || configured[device] < shape.smem) {
+            static std::atomic<size_t> configured[64];  // largest opt-in set per device
+            if (device >= 64 || configured[device].load(std::memory_order_relaxed) < shape.smem) {
                 cuda_check(cudaFuncSetAttribute(gather_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                 static_cast<int>(shape.smem)),
                            "configure bulk gather shared memory");
-                if (device < 64) configured[device] = shape.smem;
+                if (device < 64) configured[device].store(shape.smem, std::memory_order_relaxed);
             }
             const int64_t needed = (n_rows + kBulkWarps - 1) / kBulkWarps;
             const int64_t sms = sm_count(device);

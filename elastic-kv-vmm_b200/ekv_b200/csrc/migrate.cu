@@ -13,6 +13,7 @@
 // (posted writes for demotion, so the SMs never wait on the link for it).
 // A warp moves one row per step with kUnroll vectors per lane in flight; the
 // grid is persistent.
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -97,11 +98,11 @@ row_copy_kernel(const __grid_constant__ RowCopyParams p) {
 }
 
 int copy_grid(int device, int64_t n_tasks) {
-    static int cached[64] = {0};
-    int grid = device < 64 ? cached[device] : 0;
+    static std::atomic<int> cached[64];  // per device; a race computes twice
+    int grid = device < 64 ? cached[device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
         grid = persistent_grid(reinterpret_cast<const void*>(row_copy_kernel), kCopyThreads, 0, device);
-        if (device < 64) cached[device] = grid;
+        if (device < 64) cached[device].store(grid, std::memory_order_relaxed);
     }
     const int64_t needed = (n_tasks + kCopyWarps - 1) / kCopyWarps;
     return static_cast<int>(needed < grid ? needed : grid);
