@@ -47,3 +47,27 @@ def test_bench_arguments():
     assert args.warmup >= 3
     args = bench.parse_args(["--gpus", "8", "--steps", "7", "--warmup", "4", "--only", "shadow"])
     assert (args.gpus, args.steps, args.warmup, args.only) == (8, 7, 4, "shadow")
+
+
+def test_config5_topk_schedule_properties():
+    """The config-5 Top-K schedule: int32 [steps, batch, k], distinct ids in [0, context)
+    per row, each step keeping at least keep * k of the previous step's ids, new ids
+    Zipf-concentrated near the newest token, and the same schedule for the same seed."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    steps, batch, context, k, keep = 5, 3, 65536, 512, 0.9
+    sched = bench.zipf_topk_schedule(steps, batch, context, k, keep, 1.1, seed=11)
+    assert sched.shape == (steps, batch, k) and sched.dtype == np.int32
+    assert ((sched >= 0) & (sched < context)).all()
+    for t in range(steps):
+        for b in range(batch):
+            assert len(set(sched[t, b].tolist())) == k
+            if t:
+                shared = set(sched[t, b].tolist()) & set(sched[t - 1, b].tolist())
+                assert len(shared) >= int(k * keep)
+    distance = context - 1 - sched[0].astype(np.int64)
+    assert np.median(distance) < context // 8  # Zipf(1.1) over distance from the newest token
+    assert np.array_equal(sched, bench.zipf_topk_schedule(steps, batch, context, k, keep, 1.1, seed=11))
