@@ -18,12 +18,19 @@ chunks with permuted slots; host-link GB/s per direction; plus the commit path a
 forced demote + promote round trip through the transaction API at the size of the
 reference's published case), ``lookup``
 (config 1 lookups, resolve_resident at the reference's microbenchmark shape,
-shared-prefix donor resolution at the config-5 shape), ``shadow`` (logical-shadow
+shared-prefix donor resolution at the config-5 shape, the reference's single-plane
+gather_rows at one TP8 layer plane), ``shadow`` (logical-shadow
 bitwise check of one decode step at the config-2 batch, vs the reference's torch body
 on the same GPU), ``bitmap`` (config 4
 geometry: freeable bitmap build, the NCCL AND-combine latency and, for N > 1,
 the fused peer-memory combine), ``clocks`` (NVML samples during the timed
 region).
+
+``--config 4`` / ``--config 5`` time the decode-step configurations instead (one
+JSON line each): config 4 reports its concurrent form (each layer's lookup beside
+its mapped gather) with the plain layer order and the Top-K-ahead pipelined order
+in ``step_forms``; config 5 reports the swap-in pipeline with the plain layer
+order as ``sequential_ms_per_step``.
 
 ``--impl reference`` times the reference's CPU path (torch-CPU restatement,
 all host threads) on a bounded sample of the same workload.
