@@ -586,3 +586,64 @@ def test_peer_combiner_checks_its_arguments():
         combiner.combine(local_bits=torch.zeros(2, dtype=torch.int64), out=torch.zeros(2, dtype=torch.int64))
     with pytest.raises(ValueError, match="rank is required"):
         PeerFreeableCombiner(100, "cpu", buffers=[0x1000])
+
+
+def _fake_pipeline_torch(log):
+    """A stand-in for the torch.cuda calls LayerPipeline makes, recording each one."""
+    import types
+
+    import torch
+
+    class Stream:
+        def __init__(self, name="side"):
+            self.name = self.cuda_stream = name
+
+        def wait_stream(self, other):
+            log.append(("wait_stream", self.name, other.name))
+
+        def wait_event(self, event):
+            log.append(("wait_event", self.name, event.id))
+
+    class Event:
+        made = 0
+
+        def __init__(self):
+            Event.made += 1
+            self.id = Event.made
+
+        def record(self, stream):
+            log.append(("record", self.id, stream.name))
+
+    main = Stream("main")
+    cuda = types.SimpleNamespace(Stream=lambda device: Stream("side"), Event=Event,
+                                 current_stream=lambda device: main)
+    return types.SimpleNamespace(cuda=cuda, device=torch.device)
+
+
+@pytest.mark.parametrize("wait", [True, False])
+def test_layer_pipeline_stream_order(wait, monkeypatch):
+    """LayerPipeline's schedule, recorded through fake streams and events.  wait=True:
+    producers on the caller's stream, consumer i on the second stream after an event
+    recorded behind producer i.  wait=False: consumers on the caller's stream, producer i
+    forked onto the second stream behind everything issued before layer i (so after
+    consumer i-1, not after consumer i).  Both fork first and join once at the end."""
+    from ekv_b200 import pipeline
+
+    log = []
+    monkeypatch.setattr(pipeline, "torch", _fake_pipeline_torch(log))
+    layers = 3
+    produce = [lambda s, i=i: log.append(("produce", i, s)) for i in range(layers)]
+    consume = [lambda s, i=i: log.append(("consume", i, s)) for i in range(layers)]
+    step = pipeline.LayerPipeline(produce, consume, "cpu", wait=wait)
+    event = {i: step.ready[i].id for i in range(layers)}
+    step()
+    want = [("wait_stream", "side", "main")]
+    for i in range(layers):
+        if wait:
+            want += [("produce", i, "main"), ("record", event[i], "main"), ("wait_event", "side", event[i]),
+                     ("consume", i, "side")]
+        else:
+            want += [("record", event[i], "main"), ("wait_event", "side", event[i]), ("produce", i, "side"),
+                     ("consume", i, "main")]
+    want.append(("wait_stream", "main", "side"))
+    assert log == want
