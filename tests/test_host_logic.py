@@ -647,3 +647,26 @@ def test_layer_pipeline_stream_order(wait, monkeypatch):
                      ("consume", i, "main")]
     want.append(("wait_stream", "main", "side"))
     assert log == want
+
+
+def test_swap_pipeline_is_the_waiting_layer_pipeline(monkeypatch):
+    """SwapPipeline runs each plan's swap-in as the producer and its gather as the
+    consumer, in the waiting form (the gather reads the rows the swap-in promoted)."""
+    import types
+
+    from ekv_b200 import pipeline, swap
+
+    log = []
+    monkeypatch.setattr(pipeline, "torch", _fake_pipeline_torch(log))
+
+    def plan(i):
+        return types.SimpleNamespace(device="cpu", swap_in=lambda s: log.append(("swap_in", i, s)),
+                                     gather=lambda s: log.append(("gather", i, s)))
+
+    step = swap.SwapPipeline([plan(0), plan(1)])
+    assert step.wait
+    step()
+    calls = [entry for entry in log if entry[0] in ("swap_in", "gather")]
+    assert calls == [("swap_in", 0, "main"), ("gather", 0, "side"), ("swap_in", 1, "main"), ("gather", 1, "side")]
+    with pytest.raises(ValueError, match="at least one layer"):
+        swap.SwapPipeline([])
