@@ -111,3 +111,19 @@ def test_compiled_binding_loads_and_declines_cpu_tensors(library_path):
     # Empty selections are no-ops on both paths.
     empty = torch.zeros((2, 0), dtype=torch.int64)
     assert binding.gather_rows(raw, empty, ids, lens, None, None, out[:, :0], 4, 8, 32, 0, False) == 0
+
+
+def test_compiled_binding_can_be_turned_off(library_path):
+    """EKV_B200_NO_TORCH_BINDING=1 leaves every call on the checked ctypes path (checked in
+    a child process: the binding is loaded once per process)."""
+    import os
+    import subprocess
+    import sys
+
+    from conftest import PACKAGE_ROOT, ROOT
+
+    code = "from ekv_b200 import _lib; assert _lib.torch_binding() is None; print('off')"
+    env = dict(os.environ, EKV_B200_NO_TORCH_BINDING="1",
+               PYTHONPATH=os.pathsep.join([str(PACKAGE_ROOT), str(ROOT)]))
+    done = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert done.returncode == 0 and done.stdout.strip() == "off", done.stderr[-2000:]
