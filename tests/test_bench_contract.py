@@ -71,3 +71,35 @@ def test_config5_topk_schedule_properties():
     distance = context - 1 - sched[0].astype(np.int64)
     assert np.median(distance) < context // 8  # Zipf(1.1) over distance from the newest token
     assert np.array_equal(sched, bench.zipf_topk_schedule(steps, batch, context, k, keep, 1.1, seed=11))
+
+
+def test_clock_sampler_decodes_reasons(monkeypatch):
+    """ClockSampler with a fake NVML: the median SM clock of the samples taken in the
+    region, the max clock, and every clock-event reason bit seen (here sw_power_cap and
+    hw_slowdown) by name."""
+    import time
+    import types
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    clocks = iter([1965, 1950, 1965, 1800] + [1965] * 1000)
+    bits = iter([0x4, 0x0, 0x4 | 0x8] + [0x0] * 1000)
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=0, nvmlInit=lambda: None, nvmlDeviceGetHandleByIndex=lambda index: index,
+        nvmlDeviceGetMaxClockInfo=lambda handle, kind: 1965,
+        nvmlDeviceGetClockInfo=lambda handle, kind: next(clocks),
+        nvmlDeviceGetCurrentClocksEventReasons=lambda handle: next(bits))
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    with bench.ClockSampler(0, period=0.001) as sampler:
+        while len(sampler.samples) < 4:
+            time.sleep(0.005)
+    summary = sampler.summary()
+    assert summary["sm_max_mhz"] == 1965 and summary["samples"] >= 4
+    assert {"sw_power_cap", "hw_slowdown"} <= set(summary["reasons"])
+    assert set(summary["reasons"]) <= {"sw_power_cap", "hw_slowdown"}
+    # Without NVML the sampler reports no clocks instead of guessing.
+    monkeypatch.setitem(sys.modules, "pynvml", None)
+    with bench.ClockSampler(0) as silent:
+        pass
+    assert silent.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
