@@ -308,3 +308,72 @@ def test_shadow_check_complete_oracle_matches_reference(case):
                                 c["logical"], c["physical"], page, size, live, int(c["capacity"]))
     np.testing.assert_array_equal(counts, c["counts"])
     assert bool(c["raised"]) == bool(counts[2] or counts[3])
+
+
+# --------------------------------------------------------------------------- swap-in (this build's policy)
+
+from oracle import swap as osw  # noqa: E402
+
+
+def _inverse(res_map, slot_token):
+    for b in range(res_map.shape[0]):
+        tokens = np.nonzero(res_map[b] >= 0)[0]
+        assert (slot_token[b, res_map[b, tokens]] == tokens).all()
+        slots = np.nonzero(slot_token[b] >= 0)[0]
+        assert (res_map[b, slot_token[b, slots]] == slots).all()
+
+
+def test_swap_oracle_invariants_over_decode_steps():
+    """The clock victim policy the swap kernels implement, over 8 decode steps: the map
+    and the slot table stay inverse, hits keep their slots, victims come in ring order
+    from the hand, and after promotion every Top-K row reads its history row."""
+    rng = np.random.default_rng(61)
+    batch, context, hot, k, width = 3, 400, 48, 32, 4
+    res_map = np.full((batch, context), -1, dtype=np.int32)
+    slot_token = np.full((batch, hot), -1, dtype=np.int32)
+    hand = np.zeros(batch, dtype=np.int32)
+    history = rng.integers(-30000, 30000, (batch * context, width)).astype(np.int16)
+    hot_rows = np.zeros((batch, hot, width), dtype=np.int16)
+    lengths = np.full(batch, context)
+    topk = np.stack([rng.choice(context, k, replace=False) for _ in range(batch)]).astype(np.int32)
+    for _ in range(8):
+        slots, miss, miss_list, miss_count = ol.lookup_slots(res_map, topk)
+        before_hand = hand.copy()
+        hits = {(b, int(t)): int(s) for b in range(batch) for t, s in zip(topk[b], slots[b]) if s >= 0}
+        promo = osw.swap_select(res_map, slot_token, hand, slots, miss_list, miss_count)
+        _inverse(res_map, slot_token)
+        for (b, t), s in hits.items():
+            assert res_map[b, t] == s  # a hit is never evicted in its own step
+        for b in range(batch):
+            n = int(miss_count[b])
+            got = promo[b, :n]
+            assert (got >= 0).all() and len(set(got.tolist())) == n
+            ring = (before_hand[b] + np.arange(hot)) % hot
+            free = [s for s in ring if s not in set(slots[b][slots[b] >= 0].tolist())]
+            assert got.tolist() == free[:n]  # ring order from the hand, referenced slots skipped
+        osw.promote_rows(history, hot_rows, miss_list, miss_count, promo, context)
+        out = osw.mapped_gather(hot_rows, res_map, topk, lengths)
+        rows = np.arange(batch)[:, None] * context + topk
+        np.testing.assert_array_equal(out, history[rows])
+        keep = topk[:, : k * 3 // 4]  # 75 % of the ids stay, the rest are new
+        fresh = [rng.choice(np.setdiff1d(np.arange(context), keep[b]), k - keep.shape[1], replace=False)
+                 for b in range(batch)]
+        topk = np.concatenate([keep, np.stack(fresh)], axis=1).astype(np.int32)
+
+
+def test_swap_oracle_assigns_only_free_slots():
+    """More misses than unreferenced slots: the free slots are assigned in ring order,
+    the rest of promo_slot stays -1 and the hand does not move."""
+    res_map = np.full((1, 20), -1, dtype=np.int32)
+    slot_token = np.full((1, 4), -1, dtype=np.int32)
+    res_map[0, [3, 5]] = [0, 2]
+    slot_token[0, [0, 2]] = [3, 5]
+    hand = np.array([1], dtype=np.int32)
+    topk = np.array([[3, 5, 7, 8, 9]], dtype=np.int32)
+    slots, _, miss_list, miss_count = ol.lookup_slots(res_map, topk)
+    assert miss_count.tolist() == [3]
+    promo = osw.swap_select(res_map, slot_token, hand, slots, miss_list, miss_count)
+    assert promo[0].tolist() == [1, 3, -1, -1, -1]
+    assert hand.tolist() == [1]
+    assert res_map[0, [3, 5, 7, 8, 9]].tolist() == [0, 2, 1, 3, -1]
+    _inverse(res_map, slot_token)
