@@ -194,16 +194,24 @@ def library(path: str | None = None) -> ct.CDLL:
             f"libekv_b200.so could not be loaded from {path}; build it with "
             "`python -m ekv_b200.build` (nvcc, sm_100a). There is no fallback path."
         ) from exc
+    def entry(name):
+        try:
+            return getattr(lib, name)
+        except AttributeError:
+            raise RuntimeError(
+                f"{path} does not export {name}: it is older than this package (its ABI is "
+                "outdated); rebuild it with `python -m ekv_b200.build`") from None
+
     for name, argtypes in _KERNELS.items():
-        fn = getattr(lib, name)
+        fn = entry(name)
         fn.argtypes = argtypes
         fn.restype = ct.c_int
-    lib.ekv_error.argtypes = []
+    entry("ekv_error").argtypes = []
     lib.ekv_error.restype = ct.c_char_p
-    lib.ekv_abi_version.argtypes = []
+    entry("ekv_abi_version").argtypes = []
     lib.ekv_abi_version.restype = ct.c_int
     for name, (argtypes, restype) in _VMM.items():
-        fn = getattr(lib, name)
+        fn = entry(name)
         fn.argtypes = argtypes
         fn.restype = restype
     return lib

@@ -233,7 +233,12 @@ class Backing:
         return len(pending)
 
     def close(self):
-        """Close once no tensor view, kernel or transfer can touch the backing."""
+        """Close once no tensor view, kernel or transfer can touch the backing.
+
+        ``ev_close`` frees the native handle even when the teardown fails, so a
+        failed close raises once and leaves the backing poisoned without a handle;
+        a later ``close`` (or the finalizer) does not call ``ev_close`` again.
+        """
         handle = self._handle
         if handle:
             if self._lib.ev_close(handle):

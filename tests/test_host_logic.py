@@ -265,6 +265,9 @@ class FakeLibrary:
 
     def ev_close(self, handle):
         self.calls.append(("ev_close", []))
+        if self.fail == "ev_close":
+            self.error = b"ev_close failed"
+            return -1
         return 0
 
 
@@ -303,6 +306,32 @@ def test_backing_clean_failure_stays_usable_and_poison_stops_it():
         backing.reclaim({1}, synchronize=False)
     with pytest.raises(RuntimeError, match="closed or has encountered"):
         backing.ensure({2})
+
+
+def test_backing_failed_close_is_final():
+    """ev_close frees its handle even when the teardown fails, so a failed close leaves
+    the backing poisoned with no handle: it raises once, and neither a second close nor
+    the garbage-collection finalizer calls ev_close on the freed handle again."""
+    import gc
+
+    lib = FakeLibrary()
+    backing = Backing(8 << 20, 2 << 20, device=0, library=lib)
+    backing.ensure({1})
+    lib.fail = "ev_close"
+    with pytest.raises(RuntimeError, match="teardown failed: ev_close failed"):
+        backing.close()
+    with pytest.raises(RuntimeError, match="closed or has encountered"):
+        backing.ensure({2})
+    backing.close()
+    del backing
+    gc.collect()
+    assert [c for c in lib.calls if c[0] == "ev_close"] == [("ev_close", [])]
+    # A backing dropped without close is closed once by its finalizer.
+    lib2 = FakeLibrary()
+    dropped = Backing(8 << 20, 2 << 20, device=0, library=lib2)
+    del dropped
+    gc.collect()
+    assert [c for c in lib2.calls if c[0] == "ev_close"] == [("ev_close", [])]
 
 
 def test_backing_spare_handles():
@@ -449,6 +478,25 @@ def test_library_missing_fails_loudly(tmp_path):
 
     with pytest.raises(RuntimeError, match="no fallback"):
         _lib.library(str(tmp_path / "missing.so"))
+
+
+def test_library_without_the_entry_points_asks_for_a_rebuild(tmp_path):
+    """A shared library that loads but lacks this package's entry points (an older build)
+    is refused with a rebuild instruction, not an AttributeError from ctypes."""
+    import shutil
+    import subprocess
+
+    from ekv_b200 import _lib
+
+    compiler = shutil.which("gcc") or shutil.which("cc")
+    if compiler is None:
+        pytest.skip("no C compiler")
+    source = tmp_path / "old.c"
+    source.write_text("int ekv_unrelated(void) { return 0; }\n")
+    stale = tmp_path / "libold.so"
+    subprocess.run([compiler, "-shared", "-fPIC", "-o", str(stale), str(source)], check=True)
+    with pytest.raises(RuntimeError, match="ABI is outdated"):
+        _lib.library(str(stale))
 
 
 def test_ctypes_arrays():
