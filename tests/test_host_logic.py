@@ -461,6 +461,49 @@ def test_profile_ranges_env_is_read_at_decoration(monkeypatch):
     assert wrapped is not fn and wrapped() == 3
 
 
+def test_profile_ranges_nest_and_let_exceptions_through(monkeypatch):
+    """Enabled ranges enter and exit in nesting order around each call, an exception
+    raised inside propagates unchanged through both ranges, and the wrapper keeps the
+    function's name (the behaviour tests/test_profile_ranges.py:24-50 of the reference
+    pins)."""
+    import contextlib
+
+    import torch
+
+    from ekv_b200.profile_ranges import profile_range
+
+    events = []
+
+    @contextlib.contextmanager
+    def record_function(name):
+        events.append(("enter", name))
+        try:
+            yield
+        finally:
+            events.append(("exit", name))
+
+    monkeypatch.setenv("EKV_PROFILE_RANGES", "1")
+    monkeypatch.setattr(torch.profiler, "record_function", record_function)
+    expected = ValueError("bad input")
+
+    @profile_range("test/inner")
+    def inner(*, fail):
+        if fail:
+            raise expected
+        return 7
+
+    @profile_range("test/outer")
+    def outer(fail):
+        return inner(fail=fail)
+
+    assert outer(False) == 7
+    with pytest.raises(ValueError) as caught:
+        outer(True)
+    assert caught.value is expected and inner.__name__ == "inner"
+    assert events == [("enter", "ekv/test/outer"), ("enter", "ekv/test/inner"),
+                      ("exit", "ekv/test/inner"), ("exit", "ekv/test/outer")] * 2
+
+
 def test_no_cpu_fallback_without_cuda_tensors():
     from ekv_b200.resident_lookup import lookup_slots, resolve_resident
 
