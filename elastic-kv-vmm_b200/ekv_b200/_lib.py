@@ -157,7 +157,6 @@ _KERNELS = {
         _p,
     ],
     "ekv_shadow_reset": [_u64p, _i32, _i64, _p, _i32, _i64, _i32, _p],
-    "ekv_device_status": [_i32, ct.POINTER(ct.c_uint), _i32],
 }
 
 _VMM = {
@@ -175,6 +174,8 @@ _VMM = {
     "ev_spare": ([_p], ct.c_uint64),
     "ev_error": ([], ct.c_char_p),
 }
+
+ABI_VERSION = 2  # EKV_ABI_VERSION of include/ekv_kernels.h
 
 EXPORTS = tuple(_KERNELS) + ("ekv_error", "ekv_abi_version") + tuple(_VMM)
 
@@ -210,6 +211,10 @@ def library(path: str | None = None) -> ct.CDLL:
     lib.ekv_error.restype = ct.c_char_p
     entry("ekv_abi_version").argtypes = []
     lib.ekv_abi_version.restype = ct.c_int
+    if lib.ekv_abi_version() != ABI_VERSION:
+        raise RuntimeError(
+            f"{path} has ABI version {lib.ekv_abi_version()}, this package needs {ABI_VERSION}; "
+            "rebuild it with `python -m ekv_b200.build`")
     for name, (argtypes, restype) in _VMM.items():
         fn = entry(name)
         fn.argtypes = argtypes
@@ -258,14 +263,6 @@ def call(name: str, *args) -> None:
     lib = library()
     if getattr(lib, name)(*args) != 0:
         raise KernelError(f"{name}: {lib.ekv_error().decode('utf-8', 'replace')}")
-
-
-def device_status(device, clear: bool = True) -> int:
-    """Sticky status word of ``device`` (0 = every bounded wait completed); synchronous."""
-    index = torch.device(device).index if not isinstance(device, int) else device
-    status = ct.c_uint(0)
-    call("ekv_device_status", 0 if index is None else index, ct.byref(status), int(clear))
-    return status.value
 
 
 def u64_array(values) -> ct.Array:

@@ -56,4 +56,4 @@ bool dependent_launch_enabled() {
 
 extern "C" const char* ekv_error(void) { return ekv::g_last_error.c_str(); }
 
-extern "C" int ekv_abi_version(void) { return 1; }
+extern "C" int ekv_abi_version(void) { return EKV_ABI_VERSION; }

@@ -17,13 +17,12 @@
 // above the HBM bandwidth-latency product without adding so many concurrent
 // random streams that DRAM efficiency drops.  The grid is persistent: SMs x
 // resident blocks.  Rows whose addresses are not 16-byte aligned fall back to
-// the widest element size that divides every address.  A bulk-copy (TMA
-// engine) variant is kept for comparison; see bulk_allowed().
+// the widest element size that divides every address.  (A bulk-copy, TMA
+// engine, variant measured 0.89 of the copy peak at 2 KiB rows and was bound by
+// the bulk-operation rate at smaller rows, so the register-staged kernel is the
+// only one.)
 #include <atomic>
-#include <cstdlib>
-#include <cstring>
 
-#include "bulk.cuh"
 #include "common.cuh"
 
 namespace ekv {
@@ -39,7 +38,8 @@ struct GatherParams {
     int64_t table_width, request_stride, sink_elements;
     uint64_t plane_or;  // OR of all plane base addresses, for the alignment test
     int pos_es, req_es, len_es, table_es, off_es;
-    int indirect;
+    int indirect;       // addressing mode: 0 direct, 1 indirect, 2 mapped
+    int indices_ready;  // EKV_GATHER_INDICES_READY was set: see first_batch()
     int n_planes;
     int vec_shift;  // log2(row_bytes / 16) when that is a power of two, else -1
     const char* src[EKV_MAX_PLANES];
@@ -56,9 +56,6 @@ struct GatherParams {
 #endif
 #ifndef EKV_GATHER_UNROLL
 #define EKV_GATHER_UNROLL 8      // 16-byte vectors in flight per lane
-#endif
-#ifndef EKV_GATHER_BATCH_RESOLVE
-#define EKV_GATHER_BATCH_RESOLVE 1  // resolve 32 rows' index chains at once (one per lane)
 #endif
 
 constexpr int kGatherThreads = 256;
@@ -234,10 +231,35 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
     }
 }
 
-// Rows are taken 32 at a time per warp (row0 + k * warps, k < 32): every lane
-// resolves one row's index chain, so the three dependent index loads are paid
-// once per 32 rows instead of once per row; the warp then streams each row out
-// of all planes with the offset broadcast from its lane.
+// Offset of row row0 + lane * warps in every source plane, or -1 for a zero row
+// (invalid position, or a row past the end).  Each lane resolves one row of the
+// warp's 32-row batch, so the three dependent index loads are paid once per 32 rows.
+__device__ __forceinline__ int64_t resolve_batch(const GatherParams& p, int64_t row0, int64_t warps,
+                                                 int64_t n_rows, unsigned lane) {
+    const int64_t r = row0 + static_cast<int64_t>(lane) * warps;
+    bool valid = false;
+    int64_t src = 0;
+    if (r < n_rows) src = resolve_row(p, r, valid);
+    return valid ? src : -1;
+}
+
+// The first batch's index chain.  With `indices_ready` the caller has promised
+// that the kernel launched just before this one in the stream does not write the
+// index inputs (positions, request ids, lengths, table, offsets), so the chain is
+// walked while that kernel drains and only the payload copy waits for it;
+// otherwise everything waits.  Either way no global store happens before the wait.
+__device__ __forceinline__ int64_t first_batch(const GatherParams& p, int64_t row0, int64_t warps,
+                                               int64_t n_rows, unsigned lane) {
+    int64_t mine = -1;
+    if (p.indices_ready) mine = resolve_batch(p, row0, warps, n_rows, lane);
+    grid_dependency_wait();
+    allow_dependents();
+    if (!p.indices_ready) mine = resolve_batch(p, row0, warps, n_rows, lane);
+    return mine;
+}
+
+// Rows are taken 32 at a time per warp (row0 + k * warps, k < 32); the warp then
+// streams each row out of all planes with the offset broadcast from its lane.
 //
 // kU: vectors in flight per lane in the flattened batch copy; kFlatAll: flatten
 // every 16-byte-aligned batch, whatever its row size (the small-row instance,
@@ -245,229 +267,157 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
 template <int kU, bool kFlatAll>
 __global__ void __launch_bounds__(kGatherThreads, kGatherBlocksPerSM)
 gather_kernel(const __grid_constant__ GatherParams p) {
-    grid_dependency_wait();
-    allow_dependents();
     const int64_t n_rows = p.batch * p.selected;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
     const unsigned lane = lane_id();
-#if !EKV_GATHER_BATCH_RESOLVE
-    for (int64_t r = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5); r < n_rows;
-         r += warps) {
-        bool valid;
-        const int64_t src = resolve_row(p, r, valid);
-        copy_row_any(p, valid, src, r * p.row_bytes, lane);
-    }
-#else
-    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5); row0 < n_rows;
-         row0 += 32 * warps) {
-        const int64_t r = row0 + static_cast<int64_t>(lane) * warps;
-        bool valid = false;
-        int64_t src = 0;
-        if (r < n_rows) src = resolve_row(p, r, valid);
-        const int64_t mine = valid ? src : -1;
+    int64_t row0 = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5);
+    int64_t mine = first_batch(p, row0, warps, n_rows, lane);
+    const bool small_rows = p.row_bytes % 16 == 0 && p.plane_or % 16 == 0 &&
+                            (kFlatAll || static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) <= kFlatRowLimit);
+    for (; row0 < n_rows; row0 += 32 * warps) {
         const int64_t left = (n_rows - row0 + warps - 1) / warps;
         const int nb = static_cast<int>(left < 32 ? left : 32);
-        const bool small_rows = p.row_bytes % 16 == 0 && p.plane_or % 16 == 0 &&
-                                (kFlatAll || static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) <= kFlatRowLimit);
-        if (small_rows && !__ballot_sync(0xffffffffu, valid && (src & 15))) {
+        if (small_rows && !__ballot_sync(0xffffffffu, mine >= 0 && (mine & 15))) {
             copy_batch_vec16<kU>(p, mine, row0, warps, nb, lane);
-            continue;
-        }
-        for (int k = 0; k < nb; ++k) {
-            const int64_t s = __shfl_sync(0xffffffffu, mine, k);
-            copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane);
-        }
-    }
-#endif
-}
-
-// ---------------------------------------------------------------- bulk (TMA engine) variant
-//
-// Each warp is an independent copy pipeline run by its lane 0: a ring of
-// `slots` shared-memory row buffers, one mbarrier per slot.  Rows come in
-// batches of 32 (one per lane): all lanes resolve their row's index chain in
-// parallel, then lane 0 streams batch-rows x planes items -- bulk load of item
-// i + lookahead into its slot, wait for item i, bulk store of item i from its
-// slot -- so ~lookahead rows per warp are in flight with no register staging.
-// A slot is refilled only after the store that last read it has finished
-// reading (bulk wait_group.read), and invalid rows are stored from a shared
-// zero row.  Every wait is bounded; an abandoned wait sets g_gather_status.
-
-constexpr int kBulkWarps = 8;
-constexpr int kBulkThreads = kBulkWarps * 32;
-constexpr int kStoreLag = 8;               // stores allowed to still read their slot when it is refilled: lag - 1
-constexpr int kMaxSlots = 32;
-constexpr uint32_t kWaitPolls = 1u << 22;  // try_wait polls before a wait is abandoned
-
-__device__ unsigned int g_gather_status;
-
-__global__ void __launch_bounds__(kBulkThreads, 1)
-gather_bulk_kernel(const __grid_constant__ GatherParams p, int slots, int slot_bytes) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    const unsigned lane = lane_id();
-    const int warp = threadIdx.x >> 5;
-    unsigned char* payload = smem;  // [warps][slots][slot_bytes]
-    unsigned char* zero_row = payload + static_cast<size_t>(kBulkWarps) * slots * slot_bytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(zero_row + slot_bytes);           // [warps][slots]
-    int64_t* row_src = reinterpret_cast<int64_t*>(bars + kBulkWarps * slots);      // [warps][32]
-
-    if (lane == 0) {
-        for (int s = 0; s < slots; ++s) bulk::mbar_init(bulk::smem_addr(bars + warp * slots + s), 1);
-    }
-    for (int i = threadIdx.x; i < slot_bytes / 16; i += kBulkThreads) {
-        reinterpret_cast<uint4*>(zero_row)[i] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    bulk::fence_barrier_init();
-    bulk::fence_async_shared();
-    __syncthreads();
-
-    const uint64_t policy = bulk::policy_evict_first();
-    const int64_t n_rows = p.batch * p.selected;
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * kBulkWarps;
-    const uint32_t row_bytes = static_cast<uint32_t>(p.row_bytes);
-    const int lookahead = slots - kStoreLag;
-    int64_t* my_src = row_src + warp * 32;
-    const uint32_t my_payload = bulk::smem_addr(payload + static_cast<size_t>(warp) * slots * slot_bytes);
-    const uint32_t my_bars = bulk::smem_addr(bars + warp * slots);
-    const uint32_t zero_addr = bulk::smem_addr(zero_row);
-    uint64_t done = 0;  // items this warp has pushed through its ring
-    bool failed = false;
-
-    for (int64_t row0 = static_cast<int64_t>(blockIdx.x) * kBulkWarps + warp; row0 < n_rows;
-         row0 += 32 * warps) {
-        const int64_t r = row0 + static_cast<int64_t>(lane) * warps;
-        int64_t src = -1;
-        bool aligned = true;
-        if (r < n_rows) {
-            bool valid;
-            const int64_t off = resolve_row(p, r, valid);
-            if (valid) {
-                src = off;
-                aligned = (off & 15) == 0;
-            }
-        }
-        const int64_t left = (n_rows - row0 + warps - 1) / warps;
-        const int nb = static_cast<int>(left < 32 ? left : 32);
-        if (__ballot_sync(0xffffffffu, !aligned)) {
-            // A row of this batch is not 16-byte aligned: vector / element copies.
+        } else {
             for (int k = 0; k < nb; ++k) {
-                const int64_t s = __shfl_sync(0xffffffffu, src, k);
+                const int64_t s = __shfl_sync(0xffffffffu, mine, k);
                 copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane);
             }
-            continue;
         }
-        my_src[lane] = src;
-        __syncwarp();
-        if (lane == 0 && !failed) {
-            const int64_t items = static_cast<int64_t>(nb) * p.n_planes;
-            int64_t issued = 0;
-            int issue_row = 0, issue_plane = 0, store_row = 0, store_plane = 0;
-            auto issue = [&]() {
-                const uint64_t g = done + issued;
-                const uint32_t slot = static_cast<uint32_t>(g % slots);
-                if (g >= static_cast<uint64_t>(slots)) bulk::wait_read<kStoreLag - 1>();
-                const uint32_t bar = my_bars + slot * 8u;
-                const int64_t s = my_src[issue_row];
-                if (s < 0) {
-                    bulk::mbar_arrive(bar);
-                } else {
-                    bulk::mbar_arrive_expect_tx(bar, row_bytes);
-                    bulk::load_async(my_payload + slot * static_cast<uint32_t>(slot_bytes),
-                                     p.src[issue_plane] + s, row_bytes, bar, policy);
-                }
-                ++issued;
-                if (++issue_plane == p.n_planes) {
-                    issue_plane = 0;
-                    ++issue_row;
-                }
-            };
-            while (issued < items && issued < lookahead) issue();
-            for (int64_t i = 0; i < items; ++i) {
-                if (issued < items) issue();
-                const uint64_t g = done + i;
-                const uint32_t slot = static_cast<uint32_t>(g % slots);
-                if (!bulk::mbar_wait_bounded(my_bars + slot * 8u, static_cast<uint32_t>((g / slots) & 1),
-                                             kWaitPolls)) {
-                    failed = true;
-                    atomicOr(&g_gather_status, 1u);
-                    for (int64_t k = i + 1; k < issued; ++k) {  // let in-flight loads land
-                        const uint64_t gk = done + k;
-                        bulk::mbar_wait_bounded(my_bars + static_cast<uint32_t>(gk % slots) * 8u,
-                                                static_cast<uint32_t>((gk / slots) & 1), kWaitPolls);
+        mine = resolve_batch(p, row0 + 32 * warps, warps, n_rows, lane);
+    }
+}
+
+// Rows of G = row_bytes / 16 vectors per plane, G a power of two of at most 32
+// (16 to 512 B rows over 16-byte aligned planes; the 256 B rows of a TP8 head
+// shard).  Lanes are grouped G per row: lane l copies vector l % G of row l / G
+// of an R = 32 / G-row group, so one load instruction moves R whole rows of one
+// plane, and a row's offset is broadcast once per row group and reused for every
+// plane -- the flattened copy above pays an integer division and a shuffle per
+// 16-byte vector, which bound it by instruction issue at these sizes (ncu:
+// warp stalls on fixed-latency dependencies and shuffles, DRAM 68 % busy).
+// Each pass keeps kRG row groups x kPL planes of loads in flight per lane
+// (instances for launches over few planes put the depth into row groups).
+template <int kRG, int kPL>
+__device__ __forceinline__ void copy_batch_grouped(const GatherParams& p, int64_t mine, int64_t row0,
+                                                   int64_t warps, int nb, unsigned lane) {
+    const int gs = p.vec_shift;
+    const int rows_per_group = 32 >> gs;
+    const int groups = (nb + rows_per_group - 1) / rows_per_group;
+    const int sub = static_cast<int>(lane >> gs);
+    const int64_t vbyte = static_cast<int64_t>(lane & ((1u << gs) - 1u)) << 4;
+    const int n_planes = p.n_planes;
+    for (int g0 = 0; g0 < groups; g0 += kRG) {
+        int64_t src[kRG];
+        bool live[kRG];
+#pragma unroll
+        for (int j = 0; j < kRG; ++j) {
+            const int k = (g0 + j) * rows_per_group + sub;  // row of the batch
+            const int64_t s = __shfl_sync(0xffffffffu, mine, k < 32 ? k : 31);
+            live[j] = k < nb;
+            src[j] = s + vbyte;  // < vbyte for a zero row
+        }
+        for (int pb = 0; pb < n_planes; pb += kPL) {
+            uint4 v[kRG][kPL];
+#pragma unroll
+            for (int j = 0; j < kRG; ++j) {
+#pragma unroll
+                for (int q = 0; q < kPL; ++q) {
+                    v[j][q] = make_uint4(0u, 0u, 0u, 0u);
+                    if (live[j] && src[j] >= vbyte && pb + q < n_planes) {
+                        v[j][q] = load_vec(reinterpret_cast<const uint4*>(p.src[pb + q] + src[j]));
                     }
-                    break;
-                }
-                const int64_t s = my_src[store_row];
-                char* dst = p.dst[store_plane] + (row0 + static_cast<int64_t>(store_row) * warps) * p.row_bytes;
-                bulk::store_async(dst, s < 0 ? zero_addr : my_payload + slot * static_cast<uint32_t>(slot_bytes),
-                                  row_bytes, policy);
-                bulk::commit();
-                if (++store_plane == p.n_planes) {
-                    store_plane = 0;
-                    ++store_row;
                 }
             }
-            done += items;
+#pragma unroll
+            for (int j = 0; j < kRG; ++j) {
+                const int64_t k = (g0 + j) * rows_per_group + sub;
+                const int64_t dst = (row0 + k * warps) * p.row_bytes + vbyte;
+#pragma unroll
+                for (int q = 0; q < kPL; ++q) {
+                    if (live[j] && pb + q < n_planes) {
+                        store_vec(reinterpret_cast<uint4*>(p.dst[pb + q] + dst), v[j][q]);
+                    }
+                }
+            }
         }
-        __syncwarp();
     }
-    if (lane == 0) bulk::wait_all();
 }
 
-struct BulkShape {
-    int slots = 0;
-    int slot_bytes = 0;
-    size_t smem = 0;
-};
-
-// Ring geometry for rows of `row_bytes`, or slots == 0 when rows are too big.
-BulkShape bulk_shape(int device, int64_t row_bytes) {
-    static std::atomic<int> optin[64];  // per device; a race queries twice
-    int limit = device < 64 ? optin[device].load(std::memory_order_relaxed) : 0;
-    if (!limit) {
-        cuda_check(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device),
-                   "query shared memory limit");
-        if (device < 64) optin[device].store(limit, std::memory_order_relaxed);
+// At most 88 registers: two of these blocks and one 512-thread lookup block
+// (40 registers) fill an SM's 64 Ki registers exactly, which the decode step's
+// concurrent form (each layer's lookup beside its gather) relies on.
+template <int kRG, int kPL>
+__global__ void __maxnreg__(88)
+gather_grouped_kernel(const __grid_constant__ GatherParams p) {
+    const int64_t n_rows = p.batch * p.selected;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
+    const unsigned lane = lane_id();
+    int64_t row0 = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5);
+    int64_t mine = first_batch(p, row0, warps, n_rows, lane);
+    for (; row0 < n_rows; row0 += 32 * warps) {
+        const int64_t left = (n_rows - row0 + warps - 1) / warps;
+        const int nb = static_cast<int>(left < 32 ? left : 32);
+        if (!__ballot_sync(0xffffffffu, mine >= 0 && (mine & 15))) {
+            copy_batch_grouped<kRG, kPL>(p, mine, row0, warps, nb, lane);
+        } else {  // a row of this batch starts off a 16-byte boundary
+            for (int k = 0; k < nb; ++k) {
+                const int64_t s = __shfl_sync(0xffffffffu, mine, k);
+                copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane);
+            }
+        }
+        mine = resolve_batch(p, row0 + 32 * warps, warps, n_rows, lane);
     }
-    BulkShape shape;
-    if (row_bytes <= 0 || row_bytes % 16 || row_bytes > (1 << 20)) return shape;
-    shape.slot_bytes = static_cast<int>((row_bytes + 127) / 128 * 128);
-    const size_t fixed = static_cast<size_t>(shape.slot_bytes) + 8u * 32u * kBulkWarps;
-    const size_t per_slot = static_cast<size_t>(kBulkWarps) * (shape.slot_bytes + 8u);
-    if (static_cast<size_t>(limit) <= fixed) return BulkShape{};
-    int slots = static_cast<int>((static_cast<size_t>(limit) - fixed) / per_slot);
-    slots = slots < kMaxSlots ? slots : kMaxSlots;
-    if (slots < kStoreLag + 2) return BulkShape{};
-    shape.slots = slots;
-    shape.smem = fixed + static_cast<size_t>(slots) * per_slot;
-    return shape;
 }
 
-// EKV_GATHER_KERNEL=bulk selects the bulk-copy kernel (comparison runs).  It is
-// not the default: each bulk copy is one TMA-engine operation, and at about
-// 28 M operations/s per SM (two per row) it trails the register-staged kernel
-// at 2 KiB rows (0.89 vs 0.96 of the copy peak) and is operation-bound at
-// smaller rows (4.5 ms per config-2 launch at any row size).
-bool bulk_allowed() {
-    const char* mode = std::getenv("EKV_GATHER_KERNEL");
-    return mode && std::strcmp(mode, "bulk") == 0;
-}
+// Sweep knobs (build time): launches over at most EKV_GATHER_GROUPED_MAX_PLANES
+// planes take the grouped copy (0 = never); the many-plane grouped instance keeps
+// EKV_GATHER_MANY_RG row groups x EKV_GATHER_MANY_PL planes in flight; with
+// EKV_GATHER_HONOR_READY 0 the indices-ready flag is ignored.
+#ifndef EKV_GATHER_GROUPED_MAX_PLANES
+#define EKV_GATHER_GROUPED_MAX_PLANES 256
+#endif
+#ifndef EKV_GATHER_MANY_RG
+#define EKV_GATHER_MANY_RG 2
+#endif
+#ifndef EKV_GATHER_MANY_PL
+#define EKV_GATHER_MANY_PL 6
+#endif
+#ifndef EKV_GATHER_HONOR_READY
+#define EKV_GATHER_HONOR_READY 1
+#endif
 
 using GatherKernel = void (*)(GatherParams);
 
-// The kernel instance for `n_planes` planes of `row_bytes` rows.
-GatherKernel gather_kernel_for(int64_t row_bytes, int n_planes, bool& small) {
-    small = kSmallRowBytes > 0 && row_bytes <= kSmallRowBytes &&
-            static_cast<uint64_t>(n_planes) * (row_bytes >> 4) > kFlatRowLimit;
+// The kernel instance for `n_planes` planes of `row_bytes` rows; `slot` names
+// it in the per-device grid cache.
+GatherKernel gather_kernel_for(const GatherParams& p, int& slot) {
+    if (p.n_planes <= EKV_GATHER_GROUPED_MAX_PLANES && p.plane_or % 16 == 0 && p.vec_shift >= 0 &&
+        p.vec_shift <= 5) {
+        if (p.n_planes <= 2) {
+            slot = 2;
+            return gather_grouped_kernel<4, 2>;
+        }
+        if (p.n_planes <= 4) {
+            slot = 3;
+            return gather_grouped_kernel<3, 4>;
+        }
+        slot = 4;
+        return gather_grouped_kernel<EKV_GATHER_MANY_RG, EKV_GATHER_MANY_PL>;
+    }
+    const bool small = kSmallRowBytes > 0 && p.row_bytes <= kSmallRowBytes &&
+                       static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) > kFlatRowLimit;
+    slot = small ? 1 : 0;
     return small ? gather_kernel<kSmallUnroll, true> : gather_kernel<kUnroll, false>;
 }
 
-int gather_grid(GatherKernel kernel, bool small, int device, int64_t n_rows) {
-    static std::atomic<int> cached[2][64];  // per instance and device; a race computes twice
-    int grid = device < 64 ? cached[small][device].load(std::memory_order_relaxed) : 0;
+int gather_grid(GatherKernel kernel, int slot, int device, int64_t n_rows) {
+    static std::atomic<int> cached[5][64];  // per instance and device; a race computes twice
+    int grid = device < 64 ? cached[slot][device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
         grid = persistent_grid(reinterpret_cast<const void*>(kernel), kGatherThreads, 0, device);
-        if (device < 64) cached[small][device].store(grid, std::memory_order_relaxed);
+        if (device < 64) cached[slot][device].store(grid, std::memory_order_relaxed);
     }
     const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
     return static_cast<int>(needed < grid ? needed : grid);
@@ -497,7 +447,11 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         check_esize(positions_esize, "positions");
         check_esize(request_ids_esize, "request_ids");
         check_esize(lengths_esize, "lengths");
-        require(indirect >= 0 && indirect <= 2, "addressing mode must be 0 (direct), 1 (indirect) or 2 (mapped)");
+        const int flags = indirect & ~3;
+        require(flags == 0 || flags == EKV_GATHER_INDICES_READY, "unknown gather flag bits");
+        const int ready = flags != 0;
+        indirect &= 3;
+        require(indirect <= 2, "addressing mode must be 0 (direct), 1 (indirect) or 2 (mapped)");
         if (indirect == 1) {
             require(request_table && slot_offsets, "indirect gather needs request_table and slot_offsets");
             check_esize(table_esize, "request_table");
@@ -526,6 +480,7 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         p.table_es = indirect ? table_esize : 8;
         p.off_es = indirect == 1 ? offsets_esize : 8;
         p.indirect = indirect;
+        p.indices_ready = EKV_GATHER_HONOR_READY ? ready : 0;
         p.n_planes = n_planes;
         p.vec_shift = (p.row_bytes % 16) ? -1 : log2_exact(p.row_bytes / 16);
         uint64_t plane_or = 0;
@@ -539,26 +494,10 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         bind_device(device);
         const int64_t n_rows = batch * selected;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        const BulkShape shape = (plane_or % 16 == 0 && bulk_allowed()) ? bulk_shape(device, p.row_bytes)
-                                                                        : BulkShape{};
-        if (shape.slots) {
-            static std::atomic<size_t> configured[64];  // largest opt-in set per device
-            if (device >= 64 || configured[device].load(std::memory_order_relaxed) < shape.smem) {
-                cuda_check(cudaFuncSetAttribute(gather_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                static_cast<int>(shape.smem)),
-                           "configure bulk gather shared memory");
-                if (device < 64) configured[device].store(shape.smem, std::memory_order_relaxed);
-            }
-            const int64_t needed = (n_rows + kBulkWarps - 1) / kBulkWarps;
-            const int64_t sms = sm_count(device);
-            const unsigned grid = static_cast<unsigned>(needed < sms ? needed : sms);
-            gather_bulk_kernel<<<grid, kBulkThreads, shape.smem, s>>>(p, shape.slots, shape.slot_bytes);
-        } else {
-            bool small = false;
-            const GatherKernel kernel = gather_kernel_for(p.row_bytes, p.n_planes, small);
-            launch_dependent(kernel, dim3(gather_grid(kernel, small, device, n_rows)), dim3(kGatherThreads), 0, s,
-                             "gather_rows launch", p);
-        }
+        int slot = 0;
+        const GatherKernel kernel = gather_kernel_for(p, slot);
+        launch_dependent(kernel, dim3(gather_grid(kernel, slot, device, n_rows)), dim3(kGatherThreads), 0, s,
+                         "gather_rows launch", p);
         check_launch("gather_rows launch");
     });
 }
@@ -599,18 +538,3 @@ extern "C" int ekv_gather_rows_planes(
                             table_esize, slot_offsets, offsets_esize, batch, selected, width,
                             table_width, request_stride, sink_elements, indirect, device, stream);
 }
-
-extern "C" int ekv_device_status(int device, unsigned int* status, int clear) {
-    return ekv::guarded([&] {
-        ekv::require(status != nullptr, "null status pointer");
-        ekv::bind_device(device);
-        ekv::cuda_check(cudaMemcpyFromSymbol(status, ekv::g_gather_status, sizeof(unsigned int)),
-                        "read device status");
-        if (clear) {
-            const unsigned int zero = 0;
-            ekv::cuda_check(cudaMemcpyToSymbol(ekv::g_gather_status, &zero, sizeof(zero)),
-                            "clear device status");
-        }
-    });
-}
-

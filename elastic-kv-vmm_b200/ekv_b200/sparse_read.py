@@ -11,6 +11,8 @@ from __future__ import annotations
 
 from ._lib import MAX_PLANES, call, index_esize, last_error, require_cuda, stream_handle, torch_binding, u64_array
 
+INDICES_READY = 16  # EKV_GATHER_INDICES_READY of include/ekv_kernels.h
+
 
 def _mode(indirect, mapped):
     """Addressing mode of the C ABI: 0 direct, 1 indirect (software table), 2 mapped."""
@@ -90,7 +92,7 @@ def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offset
 
 
 def gather_rows_planes(planes, positions, request_ids, lengths, request_table, slot_offsets,
-                       outputs, layout, *, indirect, mapped=False):
+                       outputs, layout, *, indirect, mapped=False, indices_ready=False):
     """``gather_rows`` over every plane in ``planes`` with one row selection.
 
     ``planes[p]`` and ``outputs[p]`` play the roles of ``raw`` and ``output``
@@ -103,8 +105,13 @@ def gather_rows_planes(planes, positions, request_ids, lengths, request_table, s
     row's slot in the request's fixed region (``sink + req * request_stride +
     s * width``), and ``s < 0`` reads as a zero row -- a lookup and its gather
     in one launch.
+
+    ``indices_ready=True`` promises that the kernel launched just before this
+    call on the current stream writes none of the index tensors; the gather
+    then resolves its first index batch while that kernel finishes (see
+    ``EKV_GATHER_INDICES_READY``).  The bytes written are the same either way.
     """
-    fast = torch_binding()
+    fast = None if indices_ready else torch_binding()
     if fast is not None:
         try:
             rc = fast.gather_rows_planes(planes, outputs, positions, request_ids, lengths, request_table,
@@ -152,7 +159,7 @@ def gather_rows_planes(planes, positions, request_ids, lengths, request_table, s
             itemsize, *args, batch, selected, layout.row_elements,
             table_width, layout.request_bytes // layout.itemsize,
             layout.chunk_bytes // layout.itemsize,
-            mode, device.index, stream,
+            mode | (INDICES_READY if indices_ready else 0), device.index, stream,
         )
 
 
@@ -161,10 +168,11 @@ class PlaneGather:
     the index tensors are fixed at construction, so each call only launches.
 
     The tensors passed here must outlive the object and keep their storage.
+    ``indices_ready`` as in ``gather_rows_planes``.
     """
 
     def __init__(self, planes, positions, request_ids, lengths, request_table, slot_offsets,
-                 outputs, layout, *, indirect, mapped=False):
+                 outputs, layout, *, indirect, mapped=False, indices_ready=False):
         planes = list(planes)
         outputs = list(outputs)
         if not planes or len(planes) != len(outputs) or len(planes) > MAX_PLANES:
@@ -194,7 +202,8 @@ class PlaneGather:
             *_index_args(positions, request_ids, lengths, request_table, slot_offsets, mode),
             batch, selected, layout.row_elements,
             table_width, layout.request_bytes // layout.itemsize,
-            layout.chunk_bytes // layout.itemsize, _mode(indirect, mapped), self.device.index,
+            layout.chunk_bytes // layout.itemsize,
+            mode | (INDICES_READY if indices_ready else 0), self.device.index,
         )
         self.empty = not batch or not selected
 

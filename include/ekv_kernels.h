@@ -39,14 +39,8 @@ extern "C" {
 const char* ekv_error(void);
 
 /* ABI version of this library (bumped on any signature change). */
+#define EKV_ABI_VERSION 2
 int ekv_abi_version(void);
-
-/*
- * Sticky device-side status of `device`: non-zero when a kernel abandoned a
- * bounded wait (its output is then incomplete).  Synchronous; `clear` resets
- * it.  No reference counterpart (the reference's Triton kernels never wait).
- */
-int ekv_device_status(int device, unsigned int* status, int clear);
 
 /*
  * R1 — resident lookup.  Replaces the Triton `_resolve` launch of
@@ -107,7 +101,15 @@ int ekv_lookup_slots(
  * region, -1 = absent) so a lookup and its gather are one launch.
  * Offsets, strides and width are counted in elements of `itemsize` bytes; the
  * payload is copied bit for bit.  Index arrays are contiguous.
+ *
+ * `indirect` may carry EKV_GATHER_INDICES_READY (ORed onto the mode): the caller
+ * promises that the kernel launched immediately before this one in `stream` does
+ * not write positions, request_ids, lengths, request_table or slot_offsets.  The
+ * gather then walks its first index chain while that kernel drains (programmatic
+ * dependent launch) instead of after it; payload reads and every store still wait
+ * for it.  Results are identical either way; only a broken promise can differ.
  */
+#define EKV_GATHER_INDICES_READY 16
 int ekv_gather_rows(
     const void* raw, void* out, int64_t itemsize,
     const void* positions, int positions_esize,

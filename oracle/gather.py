@@ -6,17 +6,26 @@ import numpy as np
 
 
 def row_offsets(positions, request_ids, lengths, request_table, slot_offsets, *, width,
-                table_width, request_stride, sink_elements, indirect):
+                table_width, request_stride, sink_elements, indirect, mapped=False):
     """Element offset of every (b, i) row and its validity.
 
     Restates experimental/sparse_read.py:18-30: valid iff 0 <= pos < lengths[b]
     (:22); indirect offset = slot_offsets[request_table[req * table_width + pos]]
     (:24-26); direct offset = sink + req * request_stride + pos * width (:28).
+    ``mapped`` is this build's third mode (no reference counterpart): the table
+    holds the row's slot s in the request's fixed region, valid only when
+    0 <= s and (s + 1) * width <= request_stride; offset = sink + req *
+    request_stride + s * width.
     """
     pos = positions.astype(np.int64)
     req = request_ids.astype(np.int64)[:, None]
     valid = (pos >= 0) & (pos < lengths.astype(np.int64)[:, None])
-    if indirect:
+    if mapped:
+        flat = request_table.reshape(-1).astype(np.int64)
+        slot = np.where(valid, flat[np.where(valid, req * table_width + pos, 0)], -1)
+        valid &= (slot >= 0) & ((slot + 1) * width <= request_stride)
+        offset = np.where(valid, sink_elements + req * request_stride + slot * width, 0)
+    elif indirect:
         flat = request_table.reshape(-1)
         logical = np.where(valid, flat[np.where(valid, req * table_width + pos, 0)], 0)
         offset = np.where(valid, slot_offsets.reshape(-1)[logical.astype(np.int64)].astype(np.int64), 0)
@@ -26,7 +35,7 @@ def row_offsets(positions, request_ids, lengths, request_table, slot_offsets, *,
 
 
 def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offsets, *, width,
-                table_width, request_stride, sink_elements, indirect):
+                table_width, request_stride, sink_elements, indirect, mapped=False):
     """``out[b, i, :] = raw[off : off + width]`` for valid rows, else 0 (sparse_read.py:29-30).
 
     ``raw`` is a 1-D numpy array in the payload's element type (bf16 payloads
@@ -35,7 +44,7 @@ def gather_rows(raw, positions, request_ids, lengths, request_table, slot_offset
     offset, valid = row_offsets(positions, request_ids, lengths, request_table, slot_offsets,
                                 width=width, table_width=table_width,
                                 request_stride=request_stride, sink_elements=sink_elements,
-                                indirect=indirect)
+                                indirect=indirect, mapped=mapped)
     batch, selected = positions.shape
     out = np.zeros((batch, selected, width), dtype=raw.dtype)
     vb, vi = np.nonzero(valid)

@@ -12,18 +12,6 @@ from oracle import gather as og
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["bulk", "vector"])
-def gather_kernel(request, monkeypatch, cuda_device):
-    """Run a test with the bulk (TMA-engine) kernel, then with the register-staged one."""
-    from ekv_b200._lib import device_status
-
-    monkeypatch.setenv("EKV_GATHER_KERNEL", request.param)
-    device_status(cuda_device, clear=True)
-    yield request.param
-    torch.cuda.synchronize()
-    assert device_status(cuda_device, clear=True) == 0, "a bounded wait was abandoned"
-
-
 def _layout_of(c):
     from ekv_b200.virtual_layout import VirtualKVLayout
 
@@ -38,7 +26,7 @@ def _to(a, device, dtype=None):
 
 @pytest.mark.parametrize("case", sorted(load_npz_cases("gather_golden.npz")))
 @pytest.mark.parametrize("indirect", [False, True])
-def test_gather_rows_matches_reference(case, indirect, gather_kernel, cuda_device):
+def test_gather_rows_matches_reference(case, indirect, cuda_device):
     from ekv_b200.sparse_read import gather_rows
 
     c = load_npz_cases("gather_golden.npz")[case]
@@ -79,7 +67,7 @@ def test_gather_rows_contract(cuda_device):
 @pytest.mark.parametrize("width,itemsize_dtype", [(1024, torch.bfloat16), (128, torch.bfloat16),
                                                   (3, torch.bfloat16), (64, torch.float32),
                                                   (17, torch.uint8)])
-def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, gather_kernel, cuda_device):
+def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, cuda_device):
     from ekv_b200.sparse_read import gather_rows_planes
     from ekv_b200.virtual_layout import VirtualKVLayout
 
@@ -111,7 +99,7 @@ def test_gather_rows_planes_matches_oracle(width, itemsize_dtype, gather_kernel,
         np.testing.assert_array_equal(out.cpu().view(torch.uint8).numpy().view(exp.dtype), exp)
 
 
-def test_gather_rows_planes_more_planes_than_one_launch(gather_kernel, cuda_device):
+def test_gather_rows_planes_more_planes_than_one_launch(cuda_device):
     """300 planes: split into EKV_MAX_PLANES-sized launches."""
     from ekv_b200.sparse_read import gather_rows_planes
     from ekv_b200.virtual_layout import VirtualKVLayout
@@ -133,7 +121,7 @@ def test_gather_rows_planes_more_planes_than_one_launch(gather_kernel, cuda_devi
         assert (vals[0, :3] == p).all() and (vals[0, 3] == 0).all()
 
 
-def test_gather_full_config2_property(gather_kernel, cuda_device):
+def test_gather_full_config2_property(cuda_device):
     """Config 2 at full size (36 layers x K,V pools [262144, 8, 128] bf16, 64 requests x
     2048 Top-K slots): every gathered word identifies its plane, slot and column."""
     from ekv_b200.sparse_read import gather_rows_planes
@@ -172,9 +160,9 @@ def test_gather_full_config2_property(gather_kernel, cuda_device):
         assert bool(ok.all()), f"plane {p} mismatch"
 
 
-def test_bulk_gather_falls_back_for_misaligned_rows(gather_kernel, cuda_device):
+def test_gather_falls_back_for_misaligned_rows(cuda_device):
     """16-byte aligned planes and row size, but some slot offsets land on odd elements:
-    those 32-row batches are copied with element loads, the rest with bulk copies."""
+    those 32-row batches are copied with element loads, the rest with 16-byte vectors."""
     from ekv_b200.sparse_read import gather_rows_planes
     from ekv_b200.virtual_layout import VirtualKVLayout
 
@@ -201,7 +189,7 @@ def test_bulk_gather_falls_back_for_misaligned_rows(gather_kernel, cuda_device):
         np.testing.assert_array_equal(out.view(torch.int16).cpu().numpy(), exp)
 
 
-def test_mapped_gather_reads_slots_outside_the_region_as_absent(gather_kernel, cuda_device):
+def test_mapped_gather_reads_slots_outside_the_region_as_absent(cuda_device):
     """Mapped mode (residency map -> slot in the request's fixed hot region): slots < 0 or
     past the region's capacity give zero rows, never bytes from outside the region."""
     from ekv_b200.sparse_read import gather_rows_planes
@@ -235,7 +223,7 @@ def test_mapped_gather_reads_slots_outside_the_region_as_absent(gather_kernel, c
 
 @pytest.mark.parametrize("graph", [False, True])
 @pytest.mark.parametrize("form", ["pipelined", "concurrent"])
-def test_layer_pipeline_lookup_then_gather(form, graph, gather_kernel, cuda_device):
+def test_layer_pipeline_lookup_then_gather(form, graph, cuda_device):
     """LayerPipeline over per-layer (lookup, gather) pairs -- the config-4 decode step --
     gives every layer's slots and rows exactly as the oracle's lookup + gather.
     ``pipelined``: direct gathers of the lookup's slots, layer i's gather beside layer
@@ -323,7 +311,7 @@ def test_layer_pipeline_lookup_then_gather(form, graph, gather_kernel, cuda_devi
 
 
 
-def test_compiled_binding_serves_gathers_like_the_ctypes_path(gather_kernel, cuda_device, monkeypatch):
+def test_compiled_binding_serves_gathers_like_the_ctypes_path(cuda_device, monkeypatch):
     """gather_rows and gather_rows_planes (direct, indirect, mapped; more planes than one
     launch takes) give the same bytes through the compiled binding as through the checked
     ctypes path (forced by hiding the binding), and the same errors for malformed calls."""
@@ -403,7 +391,7 @@ def test_compiled_binding_serves_gathers_like_the_ctypes_path(gather_kernel, cud
 
 
 @pytest.mark.parametrize("indirect", [False, True])
-def test_small_rows_over_many_planes_match_the_oracle(indirect, gather_kernel, cuda_device):
+def test_small_rows_over_many_planes_match_the_oracle(indirect, cuda_device):
     """256 B rows over more planes than the default kernel instance flattens (the TP8
     shard of every layer in one launch) take the small-row instance; its bytes equal the
     oracle's, invalid positions give zero rows, and a batch holding a row that is not
@@ -436,3 +424,66 @@ def test_small_rows_over_many_planes_match_the_oracle(indirect, gather_kernel, c
                                  indirect=indirect)
     for out, exp in zip(outs, want):
         np.testing.assert_array_equal(out.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("row_bytes", [16, 32, 64, 128, 256, 512])
+@pytest.mark.parametrize("n_planes", [1, 2, 3, 7, 40])
+@pytest.mark.parametrize("mode", ["indirect", "mapped_ready"])
+def test_grouped_small_rows_match_the_oracle(row_bytes, n_planes, mode, cuda_device):
+    """Rows of 16 to 512 B (a power-of-two number of 16-byte vectors) take the grouped
+    copy, one instance per plane-count class: every byte equals the oracle's for ragged
+    batches (rows not a multiple of 32), invalid positions, empty requests and, in the
+    indirect case, a batch holding a row that starts off a 16-byte boundary (element
+    copy fallback).  The mapped case also sets the indices-ready flag, whose only
+    effect is when the index chain is walked."""
+    from ekv_b200.sparse_read import PlaneGather, gather_rows_planes
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    width = row_bytes // 2
+    gen = torch.Generator().manual_seed(row_bytes * 100 + n_planes)
+    batch, tokens, selected = 7, 96, 173
+    layout = VirtualKVLayout(batch, tokens, width, itemsize=2, chunk_bytes=4096)
+    elems = layout.capacity_bytes // 2
+    planes = [torch.randint(-30000, 30000, (elems,), generator=gen, dtype=torch.int16) for _ in range(n_planes)]
+    positions = torch.randint(-3, tokens + 3, (batch, selected), generator=gen)
+    ids = torch.randperm(batch, generator=gen)
+    lengths = torch.randint(0, tokens + 1, (batch,), generator=gen)
+    lengths[2] = 0
+    if mode == "indirect":
+        n_logical = batch * tokens
+        table = torch.randperm(n_logical, generator=gen).view(batch, tokens)
+        first = layout.chunk_bytes // 2
+        offsets = first + torch.randperm((elems - first) // width, generator=gen)[:n_logical] * width
+        offsets[table[int(ids[4]), 7]] = first + 1  # an odd element offset: off the 16-byte grid
+        positions[4, 3] = 7
+        lengths[4] = tokens
+        table_arg, indirect, mapped, ready = table, True, False, False
+    else:
+        # Residency map: token -> slot in the request's fixed region, -1 absent, some slots
+        # past the region (read as absent too).
+        rows_per_request = layout.request_bytes // row_bytes
+        table = torch.randint(-1, rows_per_request + 2, (batch, tokens), generator=gen)
+        offsets, table_arg, indirect, mapped, ready = None, table, False, True, True
+    outs = [torch.full((batch, selected, width), 9, dtype=torch.int16, device=cuda_device) for _ in planes]
+    dev_planes = [p.to(cuda_device).view(torch.bfloat16) for p in planes]
+    args = (positions.to(cuda_device), ids.to(cuda_device), lengths.to(cuda_device),
+            table_arg.to(cuda_device), None if offsets is None else offsets.to(cuda_device))
+    gather_rows_planes(dev_planes, *args, [o.view(torch.bfloat16) for o in outs], layout,
+                       indirect=indirect, mapped=mapped, indices_ready=ready)
+    again = [torch.full_like(o, 5) for o in outs]
+    PlaneGather(dev_planes, *args, [o.view(torch.bfloat16) for o in again], layout,
+                indirect=indirect, mapped=mapped, indices_ready=not ready)()
+    torch.cuda.synchronize()
+    if mapped:
+        want = og.gather_rows_planes([p.numpy() for p in planes], positions.numpy(), ids.numpy(),
+                                     lengths.numpy(), table.numpy(), None, width=width, table_width=tokens,
+                                     request_stride=layout.request_bytes // 2,
+                                     sink_elements=layout.chunk_bytes // 2, indirect=False, mapped=True)
+    else:
+        want = og.gather_rows_planes([p.numpy() for p in planes], positions.numpy(), ids.numpy(),
+                                     lengths.numpy(), table.numpy(), offsets.numpy(), width=width,
+                                     table_width=tokens, request_stride=layout.request_bytes // 2,
+                                     sink_elements=layout.chunk_bytes // 2, indirect=True)
+    for out, other, exp in zip(outs, again, want):
+        np.testing.assert_array_equal(out.cpu().numpy(), exp)
+        np.testing.assert_array_equal(other.cpu().numpy(), exp)

@@ -40,7 +40,7 @@ def test_python_binding_covers_the_headers(library_path):
 
     assert set(_lib.EXPORTS) == declared_symbols()
     lib = _lib.library(str(library_path))
-    assert lib.ekv_abi_version() == 1
+    assert lib.ekv_abi_version() == 2
     assert lib.ekv_error() == b""
 
 
