@@ -80,6 +80,8 @@ def parse_args(argv=None):
     p.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--skip-migration", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
+    p.add_argument("--skip-legs", action="store_true",
+                   help="measurement aid: skip the bitmap, lookup and shadow side legs (profiling captures)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
     p.add_argument("--only", choices=("lookup", "shadow", "bitmap", "roundtrip"), default=None,
                    help="measurement aid: run one side leg alone (no config-2 pool) and print its JSON")
@@ -452,9 +454,9 @@ def round_trip_bench(dev, reps=3, spare_chunks=0):
     = 503 MB moved per round trip (the reference's published case moved 503,347,200 B).
     Wall time includes every sync, the chunk reclaim of the demotion and the chunk
     commit of the promotion, as the reference's figure does.  The SGLang objects are
-    the package's stand-in (ekv_b200.standin); rows are checked bit for bit."""
+    the test stand-in (tests/support/standin.py); rows are checked bit for bit."""
     from ekv_b200 import migration
-    from ekv_b200.standin import install_request, migration_world
+    from tests.support.standin import install_request, migration_world
 
     world = migration_world(dev, layers=48, heads=2, head_dim=128, page_size=64, pages=2048, host_rows=8192,
                             spare_chunks=spare_chunks)
@@ -1073,9 +1075,10 @@ def run_ours(args, dist: Dist):
                                 + " -> ekv_gather_rows_planes)"}
         result["gpu_launches"] = args.steps  # the e2e loop is timed separately
 
-    result["bitmap"] = bitmap_bench(dist)
-    result["lookup"] = lookup_bench(dist)
-    result["shadow"] = shadow_bench(dist)
+    if not args.skip_legs:
+        result["bitmap"] = bitmap_bench(dist)
+        result["lookup"] = lookup_bench(dist)
+        result["shadow"] = shadow_bench(dist)
 
     if dist.rank == 0 and dist.world == 1 and not args.skip_cpu:
         result["cpu_baseline"] = cpu_baseline(work, args.cpu_seconds)
@@ -1150,9 +1153,13 @@ def run_config4(args, dist: Dist):
     # Mapped gathers read each token's slot from the residency map themselves, so they
     # need none of the lookup's output and run beside it (slots and miss list are still
     # produced for the swap-in); same rows as the direct gather of the lookup's slots.
+    # The kernel before each mapped gather on the step's stream is the previous layer's
+    # gather, which writes only the K/V outputs: the index inputs are ready, so every
+    # gather walks its first index chain while the previous one drains.
     ctx_lengths = torch.full((reqs,), ctx, dtype=torch.int64, device=dev)
     mapped = [PlaneGather(planes[2 * layer:2 * layer + 2], topks[layer], req_ids, ctx_lengths, maps[layer], None,
-                          [out_k, out_v], layout, indirect=False, mapped=True) for layer in range(layers)]
+                          [out_k, out_v], layout, indirect=False, mapped=True, indices_ready=True)
+              for layer in range(layers)]
     pipelines = {"concurrent": LayerPipeline(lookups, mapped, dev, wait=False),
                  "pipelined": LayerPipeline(lookups, gathers, dev)}
     modes = ("order", "concurrent", "pipelined")

@@ -4,8 +4,9 @@ The reference's migration transactions (adaptive_sparse/migration.py) move
 rows through SGLang's host KV pool: ``alloc_paged_token_slots``,
 ``backup_from_device_all_layer`` (migration.py:105-111), ``load_to_device_per_layer``
 (migration.py:231-234), ``allocated_host_indices`` and ``free``
-(migration.py:58-63).  ``PinnedHostKVPool`` implements exactly those methods
-on top of the pack/unpack kernels, so ``migration.py`` drives it unchanged.
+(migration.py:58-63).  ``PinnedHostKVPool`` implements those methods on top
+of the pack/unpack kernels, plus ``load_to_device_all_layer`` (every layer in
+one staged transfer), which this package's promotion uses when present.
 
 Host layout: plane-major ("layer first"): plane p (K of layer l at p = 2l,
 V at p = 2l + 1) is a region of ``capacity`` rows starting on a 2 MiB
@@ -285,6 +286,25 @@ class PinnedHostKVPool:
                 rows = host_indices.to(self.device, torch.int64).contiguous()
                 pack_rows(chunk, slots, self.buffer[first_plane * self.plane_stride:], stage_rows=rows,
                           stage_plane_stride=self.plane_stride)
+
+    def load_to_device_all_layer(self, device_pool, host_indices, device_indices, io_backend="kernel"):
+        """Copy host rows ``host_indices`` of every layer's K and V into rows ``device_indices``:
+        the inverse of ``backup_from_device_all_layer``, one staged transfer over all
+        planes instead of one per layer."""
+        layers = range(getattr(device_pool, "start_layer", 0),
+                       getattr(device_pool, "end_layer", self.layer_num))
+        planes = self._device_planes(device_pool, layers)
+        slots = device_indices.to(self.device, torch.int64).contiguous()
+        for start in range(0, len(planes), MAX_PLANES):
+            chunk = planes[start:start + MAX_PLANES]
+            first_plane = 2 * layers.start + start
+            segments = self._segments(host_indices, first_plane, len(chunk))
+            if segments is not None:
+                unpack_rows_staged(chunk, slots, self.buffer, segments)
+            else:
+                rows = host_indices.to(self.device, torch.int64).contiguous()
+                unpack_rows(chunk, slots, self.buffer[first_plane * self.plane_stride:], stage_rows=rows,
+                            stage_plane_stride=self.plane_stride)
 
     def load_to_device_per_layer(self, device_pool, host_indices, device_indices, layer_id,
                                  io_backend="kernel"):

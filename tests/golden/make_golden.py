@@ -2,7 +2,9 @@
 
 Run in a container where the reference checkout is importable:
 
-    EKV_REFERENCE=/path/to/elastic-kv-vmm TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    EKV_REFERENCE=/path/to/elastic-kv-vmm TRITON_INTERPRET=1 python tests/golden/make_golden.py [fixture ...]
+
+(with fixture names -- ``migration``, ``plan_demote_large`` -- only those are rewritten).
 
 The reference's Triton kernels (adaptive_sparse/resident_lookup.py,
 experimental/sparse_read.py) run on CPU tensors under the Triton interpreter;
@@ -458,8 +460,61 @@ def shadow_cases(ref):
     return cases
 
 
+def plan_demote_large_cases(ref):
+    """The chunk-aware retention planner on larger, denser ownership patterns than
+    ``plan_demote_cases``: many pages per chunk, several owners per chunk, long keeps."""
+    migration = ref["migration"]
+    rng = random.Random(2027)
+    cases = []
+    for trial in range(60):
+        chunk_bytes = rng.choice([128, 256, 512])
+        page_size = rng.choice([1, 2, 4])
+        row_sizes = rng.choice([[32], [32, 16], [48, 24, 24]])
+        first, planes = 0, []
+        page_count = 120
+        for plane in range(rng.randint(1, 4)):
+            row = row_sizes[plane % len(row_sizes)]
+            planes.append((first, row))
+            first += -(-((page_count + 1) * page_size * row) // chunk_bytes)
+        tracker = ref["PhysicalPages"](_FakeBacking(), page_size, page_count, planes, lambda: None,
+                                       chunk_bytes=chunk_bytes)
+        pages = rng.sample(range(1, page_count + 1), rng.randint(5, 60))
+        others = [q for q in range(1, page_count + 1) if q not in pages]
+        tracker.acquire(pages + rng.sample(others, rng.randint(0, 40)))
+        keep = rng.randint(1, len(pages))
+        os.environ["EKV_CHUNK_AWARE_RETENTION"] = "1"
+        retained, released = migration.plan_demote_pages(tracker, pages, keep)
+        os.environ.pop("EKV_CHUNK_AWARE_RETENTION", None)
+        cases.append(dict(chunk_bytes=chunk_bytes, page_size=page_size, page_count=page_count,
+                          planes=planes, owned=sorted(tracker.pages - {0}), pages=pages, keep=keep,
+                          aware=[list(retained), list(released)]))
+    return cases
+
+
+def migration_trace(ref):
+    """The reference's demote / promote transactions (adaptive_sparse/migration.py:67-288)
+    and its PhysicalPages, run over the CPU stand-in world of tests/support/standin.py:
+    every scenario of tests/support/migration_scenarios.py, recorded as a state trace."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from tests.support import migration_scenarios, standin
+
+    def make_world(**geometry):
+        return standin.migration_world("cpu", tracker_cls=ref["PhysicalPages"],
+                                       host_pool_cls=standin.CpuHostPool, **geometry)
+
+    return migration_scenarios.run_all(make_world, ref["migration"])
+
+
 def main():
     ref = _import_reference()
+    only = sys.argv[1:]
+    if only:  # e.g. `make_golden.py migration plan_demote_large`: rewrite just those fixtures
+        if "migration" in only:
+            (HERE / "migration_trace.json").write_text(json.dumps(migration_trace(ref), sort_keys=True))
+        if "plan_demote_large" in only:
+            (HERE / "plan_demote_large.json").write_text(json.dumps(plan_demote_large_cases(ref), sort_keys=True))
+        print("golden fixtures written to", HERE, only)
+        return
     np.savez_compressed(HERE / "lookup_golden.npz",
                         **{f"{case}__{key}": value for case, arrays in lookup_cases(ref).items()
                            for key, value in arrays.items()})
@@ -476,6 +531,8 @@ def main():
         dict(layouts=layout_cases(ref), releasable=releasable_cases(ref),
              plan_demote=plan_demote_cases(ref)), sort_keys=True))
     (HERE / "plans_pair12k.json").write_text(json.dumps(plans_fixture(), sort_keys=True))
+    (HERE / "plan_demote_large.json").write_text(json.dumps(plan_demote_large_cases(ref), sort_keys=True))
+    (HERE / "migration_trace.json").write_text(json.dumps(migration_trace(ref), sort_keys=True))
     print("golden fixtures written to", HERE)
 
 

@@ -761,3 +761,53 @@ def test_swap_pipeline_is_the_waiting_layer_pipeline(monkeypatch):
     assert calls == [("swap_in", 0, "main"), ("gather", 0, "side"), ("swap_in", 1, "main"), ("gather", 1, "side")]
     with pytest.raises(ValueError, match="at least one layer"):
         swap.SwapPipeline([])
+
+
+# ---------------------------------------------------------------- migration transactions vs the reference
+
+def _cpu_world(**geometry):
+    from tests.support.standin import CpuHostPool, migration_world
+
+    return migration_world("cpu", tracker_cls=PhysicalPages, host_pool_cls=CpuHostPool, **geometry)
+
+
+@pytest.mark.parametrize("scenario", ["plain", "chunk_aware", "aborts"])
+def test_transaction_logic_matches_the_reference_trace(scenario):
+    """This package's transactions and page tracker over the CPU stand-in world (host
+    rows moved by the stand-in's CPU host pool) leave the state the reference's left in
+    tests/golden/migration_trace.json, step for step.  The GPU test runs the same
+    scenarios, plus the newest-token copy, through the device data path."""
+    from tests.support import migration_scenarios as ms
+
+    want = load_json("migration_trace.json")[scenario]
+    got = (ms.aborts(_cpu_world, migration) if scenario == "aborts"
+           else ms.round_trip(_cpu_world, migration, aware=scenario == "chunk_aware"))
+    assert got == want
+
+
+def test_transaction_rejections_match_the_reference_trace():
+    from tests.support import migration_scenarios as ms
+
+    assert ms.rejections(_cpu_world, migration) == load_json("migration_trace.json")["rejections"]
+
+
+def test_newest_token_copy_needs_the_device_path():
+    """The newest token's rows are copied by the row-copy kernel: on CPU tensors the
+    promotion refuses instead of falling back to host copies."""
+    from tests.support import migration_scenarios as ms
+
+    with pytest.raises(ValueError, match="CUDA"):
+        ms.round_trip(_cpu_world, migration, aware=True, newest_on_device=True)
+
+
+@pytest.mark.parametrize("index", range(60))
+def test_plan_demote_pages_large_matches_reference(index, monkeypatch):
+    """The incremental retention planner against the reference's greedy planner on
+    denser ownership patterns (tests/golden/plan_demote_large.json)."""
+    case = load_json("plan_demote_large.json")[index]
+    tracker = PhysicalPages(FakeBacking(), case["page_size"], case["page_count"],
+                            [tuple(p) for p in case["planes"]], lambda: None, chunk_bytes=case["chunk_bytes"])
+    tracker.acquire(case["owned"])
+    monkeypatch.setenv("EKV_CHUNK_AWARE_RETENTION", "1")
+    kept, released = migration.plan_demote_pages(tracker, case["pages"], case["keep"])
+    assert [list(kept), list(released)] == case["aware"]
