@@ -26,6 +26,11 @@ geometry: freeable bitmap build, the NCCL AND-combine latency and, for N > 1,
 the fused peer-memory combine), ``clocks`` (NVML samples during the timed
 region).
 
+``config4``: config 4 (BASELINE.json's 2/4/8-GPU configuration) measured in the
+same run after the config-2 pool is released: 48 layers of lookup + K,V gather per
+decode step, then the freeable-bitmap build and its cross-rank AND-combine, all
+inside the timed step (``--skip-config4`` leaves it out).
+
 ``--config 4`` / ``--config 5`` time the decode-step configurations instead (one
 JSON line each): config 4 reports its concurrent form (each layer's lookup beside
 its mapped gather) with the plain layer order and the Top-K-ahead pipelined order
@@ -80,6 +85,7 @@ def parse_args(argv=None):
     p.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--skip-migration", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
+    p.add_argument("--skip-config4", action="store_true", help="skip the config-4 decode-step leg")
     p.add_argument("--skip-legs", action="store_true",
                    help="measurement aid: skip the bitmap, lookup and shadow side legs (profiling captures)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
@@ -400,13 +406,8 @@ def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
     aligned_d2h, _ = event_time(lambda: pack_rows_staged(planes, src, host, segments, plane_index=plane_index))
     d2h_best, d2h_med = event_time(lambda: pack_rows_staged(planes, src, host, dense_segments,
                                                             plane_index=plane_index))
-    chunk_ids = {1 + int(v) for v in victims}
-    started = time.perf_counter()
-    work.backing.reclaim(chunk_ids)
-    reclaim_s = time.perf_counter() - started
-    started = time.perf_counter()
-    work.backing.ensure(chunk_ids)
-    ensure_s = time.perf_counter() - started
+    chunk_ids = sorted({1 + int(v) for v in victims})
+    vmm = vmm_phases(work.backing, chunk_ids)
     h2d_best, h2d_med = event_time(lambda: unpack_rows_staged(planes, dst, host, dense_segments,
                                                               plane_index=plane_index))
     # The alternative layouts restore the same rows (the host image above is the
@@ -425,7 +426,14 @@ def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
     ce_h2d, _ = event_time(lambda: flat_dev.copy_(flat_host, non_blocking=True))
     ce_d2h, _ = event_time(lambda: flat_host.copy_(flat_dev, non_blocking=True))
     gbs = lambda seconds: moved / seconds / 1e9  # noqa: E731
+    first = vmm["first"]
+    vmm_s = (first["unmap_ms"] + first["release_ms"] + first["ensure_ms"]) / 1e3
     return {"victim_chunks": victims_n, "rows": n_rows, "bytes_per_direction": moved,
+            "config3_end_to_end_gbs": 2 * moved / (d2h_best + vmm_s + h2d_best) / 1e9,
+            "config3_end_to_end": "bytes moved both ways / (staged demotion + unmap + release of the victim "
+                                  "chunks + commit of fresh chunks (create, map, access, zero) + staged "
+                                  "promotion), the first round of VMM calls on this pool",
+            "vmm": vmm,
             "d2h_gbs": gbs(d2h_best), "h2d_gbs": gbs(h2d_best),
             "d2h_gbs_median": gbs(d2h_med), "h2d_gbs_median": gbs(h2d_med),
             "zero_copy_d2h_gbs": gbs(zc_d2h), "zero_copy_h2d_gbs": gbs(zc_h2d),
@@ -433,11 +441,44 @@ def migration_bench(work: Workload, victims_n: int = 256, reps: int = 3):
             "copy_engine_contiguous_d2h_gbs": gbs(ce_d2h), "copy_engine_contiguous_h2d_gbs": gbs(ce_h2d),
             "host_link_nominal_gbs": 64.0, "frac_of_nominal_d2h": gbs(d2h_best) / 64.0,
             "frac_of_nominal_h2d": gbs(h2d_best) / 64.0,
-            "reclaim_ms": reclaim_s * 1e3, "ensure_ms": ensure_s * 1e3,
+            "reclaim_ms": first["unmap_ms"] + first["release_ms"], "ensure_ms": first["ensure_ms"],
             "round_trip_bit_exact": exact, "commit_path": commit,
             "path": "staged: pack/unpack kernel into a 64 MiB device ring + copy-engine transfers on a side "
                     "stream, dense host layout (2 MiB pinned chunks, victim start rows recorded); "
                     "alternatives: per-victim 2 MiB-aligned host layout, zero-copy kernel stores/loads"}
+
+
+def vmm_phases(backing, chunk_ids, singles=8):
+    """Driver time of reclaiming and re-committing ``chunk_ids`` on a live pool, by phase.
+
+    ``single_drop_ms``: ``singles`` chunks unmapped and released one call each (the
+    latency distribution of individual drops); then, for all victims, ``unmap_ms``
+    (reclaim while spare handles are kept, so only cuMemUnmap runs), ``release_ms``
+    (cuMemRelease of the kept handles) and ``ensure_ms`` (cuMemCreate, cuMemMap,
+    cuMemSetAccess, zero fill), twice: ``first`` on the pool as the run left it,
+    ``again`` right after.
+    """
+    out = {"single_drop_ms": []}
+    for chunk in chunk_ids[:singles]:
+        started = time.perf_counter()
+        backing.reclaim({chunk}, synchronize=False)
+        out["single_drop_ms"].append((time.perf_counter() - started) * 1e3)
+    backing.ensure(chunk_ids[:singles])
+    torch.cuda.synchronize()
+    for name in ("first", "again"):
+        backing.set_spare_chunks(len(chunk_ids))
+        started = time.perf_counter()
+        backing.reclaim(chunk_ids, synchronize=False)
+        unmap = time.perf_counter() - started
+        started = time.perf_counter()
+        backing.set_spare_chunks(0)
+        release = time.perf_counter() - started
+        started = time.perf_counter()
+        backing.ensure(chunk_ids)
+        ensure = time.perf_counter() - started
+        out[name] = {"unmap_ms": unmap * 1e3, "release_ms": release * 1e3, "ensure_ms": ensure * 1e3,
+                     "chunks": len(chunk_ids)}
+    return out
 
 
 # --------------------------------------------------------------------------- lookups (config 1, R1)
@@ -483,7 +524,9 @@ def round_trip_bench(dev, reps=3, spare_chunks=0):
             after = world.backing.metrics
             samples.append((t1 - t0, t2 - t1, t2 - t0, released, {k: after[k] - before[k] for k in metric_keys}))
         destination = world.pool.full_to_hisparse_device_index_mapping[logical]
-        exact = all(bool(torch.equal(view[destination], want)) for view, want in zip(world.views, original))
+        # Bit patterns: the stand-in's seeded payload includes bf16 NaN encodings.
+        exact = all(bool(torch.equal(view[destination].view(torch.int16), want.view(torch.int16)))
+                    for view, want in zip(world.views, original))
         demote_s, promote_s, total_s, released, vmm = min(samples, key=lambda x: x[2])
         ref = REFERENCE_ROUND_TRIP
         return {"tokens": length, "layers": world.layers, "row_bytes": world.row_bytes,
@@ -903,9 +946,13 @@ def shadow_complete_bench(shadow, dev, heads, dim, capacity, reps, layers=4, pai
 
 # --------------------------------------------------------------------------- bitmap (config 4 geometry)
 
-def bitmap_bench(dist: Dist, reps: int = 50, shard: int = 0):
-    from ekv_b200.releasable import (ChunkProjection, bitmap_to_chunks, chunks_to_bitmap,
-                                     combine_freeable, freeable_bitmap)
+def freeable_world(dist: Dist, shard: int = 0):
+    """Config-4 geometry of the freeable-bitmap step: 48 layers x K,V planes over 4096
+    chunks, rows of 2048 / TP bytes, 32 requests owning the pages (page size 1), request
+    0 the demotion candidate; each rank leaves a few rank-specific chunks unmapped so
+    the cross-rank AND is not trivial.  Returns the projection, refs, mapped bitmap,
+    candidate pages and the expected joint chunk set."""
+    from ekv_b200.releasable import ChunkProjection, chunks_to_bitmap
 
     dev = dist.device
     layers, n_chunks = 48, 4096
@@ -921,10 +968,17 @@ def bitmap_bench(dist: Dist, reps: int = 50, shard: int = 0):
     owner[: slots // 8] = 0
     projection = ChunkProjection(planes, 1, CHUNK, n_chunks, dev)
     refs = projection.counts(torch.arange(slots, device=dev))
-    # Each rank has a few rank-specific unmapped chunks, so the AND is not trivial.
-    mapped_set = set(range(n_chunks)) - {(dist.rank * 37 + 5 * i) % n_chunks for i in range(8)}
-    mapped = chunks_to_bitmap(mapped_set, n_chunks, dev)
+    unmapped = {r: {(r * 37 + 5 * i) % n_chunks for i in range(8)} for r in range(dist.world)}
+    mapped = chunks_to_bitmap(set(range(n_chunks)) - unmapped[dist.rank], n_chunks, dev)
     candidate = torch.nonzero(owner == 0).flatten().to(dev)
+    return projection, refs, mapped, candidate, unmapped, n_chunks, planes_n
+
+
+def bitmap_bench(dist: Dist, reps: int = 50, shard: int = 0):
+    from ekv_b200.releasable import bitmap_to_chunks, combine_freeable, freeable_bitmap
+
+    dev = dist.device
+    projection, refs, mapped, candidate, unmapped, n_chunks, planes_n = freeable_world(dist, shard)
 
     def build():
         return freeable_bitmap(projection.counts(candidate), refs, mapped)
@@ -999,7 +1053,7 @@ def bitmap_bench(dist: Dist, reps: int = 50, shard: int = 0):
     local_set = bitmap_to_chunks(local)
     expected_joint = set(local_set)
     for r in range(dist.world):
-        expected_joint -= {(r * 37 + 5 * i) % n_chunks for i in range(8)}
+        expected_joint -= unmapped[r]
     return {"chunks": n_chunks, "words": n_chunks // 64, "ranks": dist.world,
             "freeable_local": len(local_set), "freeable_joint": len(bitmap_to_chunks(joint)),
             "joint_matches_intersection": bitmap_to_chunks(joint) == expected_joint,
@@ -1090,22 +1144,44 @@ def run_ours(args, dist: Dist):
     return result
 
 
+def run_default(args, dist: Dist):
+    """The driver's default line: config 2 (``run_ours``), then -- with the config-2 pool
+    released -- config 4, BASELINE.json's multi-GPU configuration, as the ``config4``
+    object (every rank takes part)."""
+    result = run_ours(args, dist)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if not args.skip_config4:
+        config4 = config4_leg(args, dist, args.steps, args.warmup)
+        result["config4"] = {key: value for key, value in config4.items()
+                             if key not in ("metric", "higher_is_better", "vs_baseline", "dtype", "n_gpus")}
+    return result
+
+
 CFG4 = dict(layers=48, kv_heads=8, head_dim=128, requests=32, context=131072, hot=4096, topk=2048,
             hit_fraction=0.9)
 
 
-def run_config4(args, dist: Dist):
-    """Config 4: TP-sharded sparse residency, one decode step = for each of 48 layers a
-    hot-slot lookup (R2) of that layer's Top-K followed by the gather of the hits from
-    the layer's fixed-position hot pool (direct addressing, misses read as zero rows);
-    then the freeable-bitmap AND-combine across ranks.  The 96 launches of a step are
-    replayed from one CUDA graph.  Reported: each layer's lookup and its mapped gather
-    (the gather reads slots from the residency map, not from the lookup) on two
-    streams, forked and joined per layer; timed beside it: the plain layer order
-    (lookup, then the direct gather of its slots) and the pipelined order (layer i's
-    gather beside layer i+1's lookup, which needs every Top-K up front)."""
+def config4_leg(args, dist: Dist, steps: int, warmup: int):
+    """Config 4: TP-sharded sparse residency.  One decode step = for each of 48 layers a
+    hot-slot lookup (R2) of that layer's Top-K and the gather of its K and V rows from
+    the layer's fixed-position hot pool (misses read as zero rows) into the layer's own
+    output buffers; then this rank's freeable bitmap over the config-4 chunk geometry
+    (counts + bitmap kernels) and its AND-combine across the ranks (NCCL all-gather +
+    AND kernel) -- the combine that replaces the reference's pickled all_gather_object
+    and rank_demotions intersection (scheduler_budget.py:1447-1452,
+    runtime_value.py:167-214).  The layers' launches are replayed from one CUDA
+    graph; the bitmap build and the combine, which depend on chunk ownership only,
+    run eagerly on a second stream beside them, inside the timed step (the
+    sequential form, combine after the layers, is timed too).  Reported: each
+    layer's lookup beside its mapped gather (the gather reads
+    slots from the residency map, not from the lookup); timed beside it: the plain
+    layer order (lookup, then the direct gather of its slots) and the pipelined order
+    (layer i's gather beside layer i+1's lookup, which needs every Top-K up front)."""
     import numpy as np
 
+    from ekv_b200.pipeline import LayerPipeline
+    from ekv_b200.releasable import bitmap_to_chunks, combine_freeable, freeable_bitmap
     from ekv_b200.resident_lookup import LookupPlan
     from ekv_b200.sparse_read import PlaneGather
     from ekv_b200.virtual_layout import VirtualKVLayout
@@ -1114,7 +1190,8 @@ def run_config4(args, dist: Dist):
 
     c = CFG4
     dev = dist.device
-    heads = c["kv_heads"] // (args.tp_shard or dist.world)
+    shard = args.tp_shard or dist.world
+    heads = c["kv_heads"] // shard
     width = heads * c["head_dim"]
     row_bytes = width * 2
     layers, reqs, ctx, hot, k = args.layers or c["layers"], c["requests"], c["context"], c["hot"], c["topk"]
@@ -1122,7 +1199,7 @@ def run_config4(args, dist: Dist):
     plane_elems = layout.capacity_bytes // 2
     gen = torch.Generator(device=dev).manual_seed(4)
     n_hits = int(k * c["hit_fraction"])
-    maps, topks, planes = [], [], []
+    maps, topks, planes, outs = [], [], [], []
     for _ in range(layers):
         res_map = torch.full((reqs, ctx), -1, dtype=torch.int32, device=dev)
         topk = torch.empty((reqs, k), dtype=torch.int32, device=dev)
@@ -1137,8 +1214,9 @@ def run_config4(args, dist: Dist):
             plane = torch.empty(plane_elems, dtype=torch.bfloat16, device=dev)
             torch.randn(plane.shape, generator=gen, dtype=torch.bfloat16, device=dev, out=plane)
             planes.append(plane)
-    out_k = torch.empty((reqs, k, width), dtype=torch.bfloat16, device=dev)
-    out_v = torch.empty_like(out_k)
+            # Each layer gathers into its own K / V buffers, so the written rows reach
+            # DRAM instead of being overwritten in L2 by the next layer.
+            outs.append(torch.empty((reqs, k, width), dtype=torch.bfloat16, device=dev))
     req_ids = torch.arange(reqs, device=dev)
     lengths = torch.full((reqs,), hot, dtype=torch.int64, device=dev)
     lookups, gathers = [], []
@@ -1146,60 +1224,60 @@ def run_config4(args, dist: Dist):
         plan = LookupPlan(maps[layer], topks[layer])
         lookups.append(plan)
         gathers.append(PlaneGather(planes[2 * layer:2 * layer + 2], plan.slots, req_ids, lengths, None, None,
-                                   [out_k, out_v], layout, indirect=False))
-
-    from ekv_b200.pipeline import LayerPipeline
-
+                                   outs[2 * layer:2 * layer + 2], layout, indirect=False))
     # Mapped gathers read each token's slot from the residency map themselves, so they
     # need none of the lookup's output and run beside it (slots and miss list are still
     # produced for the swap-in); same rows as the direct gather of the lookup's slots.
-    # The kernel before each mapped gather on the step's stream is the previous layer's
-    # gather, which writes only the K/V outputs: the index inputs are ready, so every
-    # gather walks its first index chain while the previous one drains.
+    # The kernel before each one on the step's stream is the previous layer's gather,
+    # which writes only K/V outputs: the index inputs are ready, so every gather walks
+    # its first index chain while the previous one drains.
     ctx_lengths = torch.full((reqs,), ctx, dtype=torch.int64, device=dev)
     mapped = [PlaneGather(planes[2 * layer:2 * layer + 2], topks[layer], req_ids, ctx_lengths, maps[layer], None,
-                          [out_k, out_v], layout, indirect=False, mapped=True, indices_ready=True)
+                          outs[2 * layer:2 * layer + 2], layout, indirect=False, mapped=True, indices_ready=True)
               for layer in range(layers)]
     pipelines = {"concurrent": LayerPipeline(lookups, mapped, dev, wait=False),
                  "pipelined": LayerPipeline(lookups, gathers, dev)}
     modes = ("order", "concurrent", "pipelined")
+    projection, refs, mapped_bits, candidate, unmapped, n_chunks, _ = freeable_world(dist, shard)
+    counts_buf = projection.counts(candidate)
+    bits_buf = freeable_bitmap(counts_buf, refs, mapped_bits)
 
     def layers_step(mode="order"):
         if mode in pipelines:
             pipelines[mode]()
-            return
-        for layer in range(layers):
-            lookups[layer]()
-            gathers[layer]()
+        else:
+            for layer in range(layers):
+                lookups[layer]()
+                gathers[layer]()
+
+    def build_bitmap():
+        freeable_bitmap(projection.counts(candidate, out=counts_buf), refs, mapped_bits, out=bits_buf)
 
     layers_step()
     torch.cuda.synchronize()
-    # Parity on layer 0 (and the last layer) against the oracle, on this rank's head shard.
+    # Parity on layer 0 and the last layer against the oracle, on this rank's head shard.
     parity = True
     for layer in sorted({0, layers - 1}):
-        lookups[layer]()
-        gathers[layer]()
-        torch.cuda.synchronize()
         slots, miss, miss_list, miss_count = ol.lookup_slots(maps[layer].cpu().numpy(), topks[layer].cpu().numpy())
         parity &= np.array_equal(lookups[layer].slots.cpu().numpy(), slots)
         parity &= np.array_equal(lookups[layer].miss_list.cpu().numpy(), miss_list)
-        for which, out in ((0, out_k), (1, out_v)):
+        for which in range(2):
             want = og.gather_rows(planes[2 * layer + which].view(torch.int16).cpu().numpy(), slots,
                                   req_ids.cpu().numpy(), lengths.cpu().numpy(), None, None, width=width,
                                   table_width=hot, request_stride=layout.request_bytes // 2,
                                   sink_elements=CHUNK // 2, indirect=False)
-            parity &= np.array_equal(out.view(torch.int16).cpu().numpy(), want)
-    # Every form of the step leaves the last layer's rows and lookup outputs of the plain one.
-    layers_step()
-    torch.cuda.synchronize()
-    plain_out = (out_k.clone(), out_v.clone())
+            parity &= np.array_equal(outs[2 * layer + which].view(torch.int16).cpu().numpy(), want)
+    # Every form of the step leaves the rows and lookup outputs of the plain one.
+    check = sorted({0, layers // 2, layers - 1})
+    plain_out = [outs[2 * layer + w].clone() for layer in check for w in range(2)]
     plain_lookup = [t.clone() for t in (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count)]
     for mode in modes[1:]:
-        for t in (out_k, out_v, lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count):
+        for t in (*outs, lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count):
             t.zero_()
         layers_step(mode)
         torch.cuda.synchronize()
-        parity &= bool(torch.equal(out_k, plain_out[0]) and torch.equal(out_v, plain_out[1]))
+        parity &= all(torch.equal(outs[2 * layer + w], plain_out[2 * i + w])
+                      for i, layer in enumerate(check) for w in range(2))
         parity &= all(torch.equal(a, b) for a, b in zip(
             (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count), plain_lookup))
     del plain_out, plain_lookup
@@ -1220,23 +1298,47 @@ def run_config4(args, dist: Dist):
         capture_error = str(exc)
     else:
         capture_error = None
-    bitmap = bitmap_bench(dist, reps=5)
 
-    from ekv_b200.releasable import combine_freeable
-
-    local = torch.zeros(64, dtype=torch.int64, device=dev)
-
-    def step(mode):
+    def replay(mode):
         if graphs:
             graphs[mode].replay()
         else:
             layers_step(mode)
-        combine_freeable(local)
+
+    joint = {}
+    main_stream = torch.cuda.current_stream(dev)
+    bitmap_stream = torch.cuda.Stream(dev)
+
+    def bitmap_and_combine():
+        build_bitmap()
+        joint["bits"] = combine_freeable(bits_buf)
+
+    def step(mode, overlap=True):
+        # The freeable bitmap and its cross-rank AND depend only on chunk ownership, not
+        # on the layers' rows: they run on a second stream beside the layers' launches
+        # and the step ends when both are done.  overlap=False runs them after the layers.
+        if not overlap:
+            replay(mode)
+            bitmap_and_combine()
+            return
+        bitmap_stream.wait_stream(main_stream)
+        with torch.cuda.stream(bitmap_stream):
+            bitmap_and_combine()
+        replay(mode)
+        main_stream.wait_stream(bitmap_stream)
 
     mode_ms = {}
     with ClockSampler(dist.local_rank) as clocks:
         for mode in modes:
-            mode_ms[mode] = timed(lambda: step(mode), args.steps, args.warmup, dist) / args.steps
+            mode_ms[mode] = timed(lambda: step(mode), steps, warmup, dist) / steps
+        sequential_ms = timed(lambda: step("concurrent", overlap=False), steps, warmup, dist) / steps
+        without_combine_ms = timed(lambda: replay("concurrent"), steps, warmup, dist) / steps
+        combine_alone_ms = timed(bitmap_and_combine, steps, warmup, dist) / steps
+    torch.cuda.synchronize()
+    expected_joint = bitmap_to_chunks(bits_buf)
+    for r in range(dist.world):
+        expected_joint -= unmapped[r]
+    joint_ok = bitmap_to_chunks(joint["bits"]) == expected_joint
     ms_per_step = mode_ms["concurrent"]
     units = reqs * k * layers
     hits = reqs * n_hits * layers
@@ -1248,14 +1350,16 @@ def run_config4(args, dist: Dist):
     achieved = bytes_per_step / (ms_per_step / 1e3) / 1e9
     result = {
         "metric": METRIC, "value": units / (ms_per_step / 1e3), "unit": "row-pairs/s",
-        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "n_gpus": dist.world, "steps": steps, "warmup": warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded residency maps, Top-K with 90% hits, N(0,1) bf16 hot pools)",
         "config": {"workload": f"config 4: TP-sharded sparse residency, {layers} layers x (lookup + K,V gather), "
                                f"{reqs} requests x {ctx} context, hot {hot}/request, Top-K {k}, "
-                               f"heads {heads}/rank, bitmap AND-combine per step",
+                               f"heads {heads}/rank, freeable bitmap + AND-combine per step",
                    "parallelism": f"tp{dist.world} (KV-head sharding; lookup replicated; NCCL AND-combine)",
-                   "cuda_graph": bool(graphs), "capture_error": capture_error},
+                   "cuda_graph": bool(graphs), "capture_error": capture_error,
+                   "l2": "no flush: each layer gathers into its own output buffers; a step touches "
+                         f"{bytes_per_step / 1e9:.2f} GB per GPU (> 126 MB L2)"},
         "step_forms": {
             "reported": "concurrent: the mapped K,V gathers (slot read from the residency map) back to back "
                         "on the step's stream, each layer's lookup (slots, miss mask, miss list) forked onto a "
@@ -1271,15 +1375,28 @@ def run_config4(args, dist: Dist):
         "hbm_gbs_per_gpu": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_source,
-                     "note": "step = 48 lookups + 48 two-plane gathers; bytes = hit rows x 4 x row_bytes "
-                             "(K and V read and written) + miss rows x 2 x row_bytes (zero rows written) + "
-                             "13 B per lookup + 4 B per miss-list entry"},
-        "parity_layer0_and_last": bool(parity), "bitmap": bitmap,
-        "gpu_launches": 2 * layers * args.steps + args.steps * (dist.world > 1),
+                     "note": f"step = {layers} lookups + {layers} two-plane gathers + bitmap build + combine; "
+                             "bytes = hit rows x 4 x row_bytes (K and V read and written) + miss rows x 2 x "
+                             "row_bytes (zero rows written) + 13 B per lookup + 4 B per miss-list entry"},
+        "combine": {"what": ("freeable-bitmap build (counts + bitmap kernels) and NCCL all_gather_into_tensor "
+                             "of each rank's 512 B bitmap + AND kernel, on a second stream beside the layers"
+                             if dist.world > 1 else "freeable-bitmap build, single rank (no exchange)"),
+                    "alone_us": combine_alone_ms * 1e3,
+                    "us_added_to_step": (ms_per_step - without_combine_ms) * 1e3,
+                    "step_without_combine_ms": without_combine_ms,
+                    "step_with_combine_after_layers_ms": sequential_ms,
+                    "freeable_joint": len(bitmap_to_chunks(joint["bits"])),
+                    "joint_matches_intersection": bool(joint_ok)},
+        "parity_layer0_and_last": bool(parity),
+        "gpu_launches": (2 * layers + 2) * steps + steps * (dist.world > 1),
         "clocks": clocks.summary(),
     }
     graphs.clear()
     return result
+
+
+def run_config4(args, dist: Dist):
+    return config4_leg(args, dist, args.steps, args.warmup)
 
 
 CFG5 = dict(layers=48, kv_heads=8, head_dim=128, requests=128, context=65536, hot=8192, topk=2048, steps=64,
@@ -1565,7 +1682,7 @@ def main(argv=None):
                 leg_result = {"lookup": lookup_bench, "shadow": shadow_bench}[args.only](dist)
             result = {"leg": args.only, **leg_result}
         else:
-            runner = {4: run_config4, 5: run_config5}.get(args.config, run_ours)
+            runner = {4: run_config4, 5: run_config5}.get(args.config, run_default)
             result = runner(args, dist)
         if dist.rank == 0:
             print(json.dumps(result), file=out, flush=True)

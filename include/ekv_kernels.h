@@ -212,8 +212,11 @@ int ekv_unpack_rows_staged(
  * of HBM for its KV pool, a host without a device allocator).  Rows must be at
  * most 2 MiB (larger ones are rejected with an error).  The first call on a
  * device looks up the ring's address with that device current: make it before
- * any stream capture.  Calls share the ring: calls that overlap on the GPU
- * race.  Calls no cudaMalloc / cudaFree.
+ * any stream capture.  That address (and the copy stream and events the staged
+ * path keeps per device) is cached for the life of the process, so resetting
+ * the device (cudaDeviceReset) after the first call is not supported.  Calls
+ * share the ring: calls that overlap on the GPU race.  Calls no cudaMalloc /
+ * cudaFree.
  */
 int ekv_pack_rows_staged_noalloc(
     const uint64_t* planes, int n_planes, int64_t row_bytes,

@@ -87,8 +87,8 @@ def test_demote_then_promote_moves_every_row(cuda_device, monkeypatch):
         assert (pool.full_to_hisparse_device_index_mapping[logical] == 0).all()
         promoted = migration.prepare_promote(c, req, torch.cuda.synchronize)
         destination = promoted.destination[:length]
-        for p, want in enumerate(original):
-            assert torch.equal(world.views[p][destination], want)
+        for p, want in enumerate(original):  # bit patterns: the seeded payload includes NaN encodings
+            assert torch.equal(world.views[p][destination].view(torch.int16), want.view(torch.int16))
         grown = migration.commit_promote(promoted, published.append, torch.cuda.synchronize)
         assert published == [row, row] and grown >= 0
         assert torch.equal(pool.full_to_hisparse_device_index_mapping[logical], destination)

@@ -67,6 +67,34 @@ def test_noalloc_staged_demotion_matches_the_allocating_entry_point(cuda_device,
         assert torch.equal(got, expected)
 
 
+def test_noalloc_staged_demotion_at_the_row_limit_and_on_a_caller_copy_stream(cuda_device, library_path):
+    """Rows of exactly 2 MiB (one row per ring slot, more rows than ring slots, so the
+    ring wraps) and a caller-supplied copy stream, each bit exact against the allocating
+    entry point."""
+    from ekv_b200.host_pool import pack_rows_staged, pinned_buffer
+
+    lib, fn = _bind(library_path)
+    gen = torch.Generator().manual_seed(77)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    for n_planes, rows, row_bytes, count, own_stream in ((2, 6, 2 << 20, 7, False), (3, 900, 4096, 700, True)):
+        planes, plane_index, slots, segments, host_size = _case(gen, cuda_device, n_planes, rows, row_bytes,
+                                                                count)
+        expected = pinned_buffer(host_size)
+        expected.fill_(0)
+        got = pinned_buffer(host_size)
+        got.fill_(0)
+        copy_stream = torch.cuda.Stream(cuda_device) if own_stream else None
+        pack_rows_staged(planes, slots, expected, segments, plane_index=plane_index, copy_stream=copy_stream)
+        addresses = (ct.c_uint64 * n_planes)(*[p.data_ptr() for p in planes])
+        rc = fn(addresses, n_planes, row_bytes, plane_index.data_ptr(), slots.data_ptr(), 8, slots.numel(),
+                ct.cast(segments.data_ptr(), ct.POINTER(ct.c_int64)), segments.shape[0],
+                got.data_ptr(), count, cuda_device.index, stream,
+                None if copy_stream is None else copy_stream.cuda_stream)
+        assert rc == 0, lib.ekv_error()
+        torch.cuda.synchronize()
+        assert torch.equal(got, expected)
+
+
 def test_noalloc_staged_demotion_rejects_rows_larger_than_a_ring_slot(cuda_device, library_path):
     lib, fn = _bind(library_path)
     plane = torch.zeros(4 << 20, dtype=torch.uint8, device=cuda_device)
