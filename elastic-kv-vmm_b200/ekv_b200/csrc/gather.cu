@@ -78,6 +78,20 @@ constexpr int kUnroll = EKV_GATHER_UNROLL;
 #ifndef EKV_GATHER_SMALL_UNROLL
 #define EKV_GATHER_SMALL_UNROLL 12
 #endif
+// Flattened batch copies find an item's row by a division per 16-byte item, or --
+// when a row has at least 32 vectors over all planes -- by walking (row, remainder)
+// forward 32 items at a time.  At 256 B rows over 36 planes the walk cut 22 % of the
+// instructions (ncu: 173 M -> 134 M) yet ran slower (0.881 vs 0.914 of the copy peak
+// over 72 planes): that launch is bound by DRAM on random 256 B rows, not by issue.
+// EKV_GATHER_WALK applies to the default instance (one layer's K and V at 2 KiB
+// rows flattens 256 vectors per row), EKV_GATHER_SMALL_WALK to the many-plane
+// small-row instance.
+#ifndef EKV_GATHER_WALK
+#define EKV_GATHER_WALK 1
+#endif
+#ifndef EKV_GATHER_SMALL_WALK
+#define EKV_GATHER_SMALL_WALK 0
+#endif
 constexpr int64_t kSmallRowBytes = EKV_GATHER_SMALL_ROW_BYTES;
 constexpr int kSmallUnroll = EKV_GATHER_SMALL_UNROLL;
 
@@ -193,12 +207,17 @@ __device__ __forceinline__ void copy_row_any(const GatherParams& p, bool valid, 
 #endif
 constexpr uint32_t kFlatRowLimit = EKV_GATHER_FLAT_LIMIT;  // vectors per row (all planes) up to which to flatten
 
-template <int kU>
+// kWalk: rows of at least 32 vectors (all planes).  Item idx = base + u * 32 + lane
+// belongs to row idx / per_row of the batch; with kWalk a lane's next item is 32
+// further on, so (row, remainder) advance with one compare instead of a division
+// per item.
+template <int kU, bool kWalk>
 __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t mine, int64_t row0,
                                                  int64_t warps, int nb, unsigned lane) {
     const uint32_t vecs = static_cast<uint32_t>(p.row_bytes >> 4);
     const uint32_t per_row = static_cast<uint32_t>(p.n_planes) * vecs;
     const uint32_t total = static_cast<uint32_t>(nb) * per_row;
+    uint32_t k = 0, rem = lane;
     for (uint32_t base = 0; base < total; base += 32 * kU) {
         uint4 v[kU];
         uint32_t row_of[kU];
@@ -206,16 +225,26 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const uint32_t idx = base + u * 32 + lane;
-            const uint32_t k = idx < total ? idx / per_row : 0;
-            const int64_t s = __shfl_sync(0xffffffffu, mine, static_cast<int>(k));
-            const uint32_t rem = idx - k * per_row;
+            if (!kWalk) {
+                k = idx < total ? idx / per_row : 0;
+                rem = idx - k * per_row;
+            }
+            const bool live = idx < total;
+            const int64_t s = __shfl_sync(0xffffffffu, mine, static_cast<int>(live ? k : 0));
             row_of[u] = k;
             rem_of[u] = rem;
             v[u] = make_uint4(0u, 0u, 0u, 0u);
-            if (idx < total && s >= 0) {
+            if (live && s >= 0) {
                 const uint32_t plane = p.vec_shift >= 0 ? (rem >> p.vec_shift) : rem / vecs;
                 const uint32_t vec = rem - plane * vecs;
                 v[u] = load_vec(reinterpret_cast<const uint4*>(p.src[plane] + s) + vec);
+            }
+            if (kWalk) {
+                rem += 32;
+                if (rem >= per_row) {
+                    rem -= per_row;
+                    ++k;
+                }
             }
         }
 #pragma unroll
@@ -265,8 +294,7 @@ __device__ __forceinline__ int64_t first_batch(const GatherParams& p, int64_t ro
 // every 16-byte-aligned batch, whatever its row size (the small-row instance,
 // whose rows x planes x vectors stay far below 2^32).
 template <int kU, bool kFlatAll>
-__global__ void __launch_bounds__(kGatherThreads, kGatherBlocksPerSM)
-gather_kernel(const __grid_constant__ GatherParams p) {
+__device__ __forceinline__ void gather_body(const GatherParams& p) {
     const int64_t n_rows = p.batch * p.selected;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
     const unsigned lane = lane_id();
@@ -278,7 +306,13 @@ gather_kernel(const __grid_constant__ GatherParams p) {
         const int64_t left = (n_rows - row0 + warps - 1) / warps;
         const int nb = static_cast<int>(left < 32 ? left : 32);
         if (small_rows && !__ballot_sync(0xffffffffu, mine >= 0 && (mine & 15))) {
-            copy_batch_vec16<kU>(p, mine, row0, warps, nb, lane);
+            // The division form for the many-plane small-row instance: its walk was
+            // slower (see EKV_GATHER_SMALL_WALK).
+            if ((kFlatAll ? EKV_GATHER_SMALL_WALK : EKV_GATHER_WALK) && p.n_planes * (p.row_bytes >> 4) >= 32) {
+                copy_batch_vec16<kU, true>(p, mine, row0, warps, nb, lane);
+            } else {
+                copy_batch_vec16<kU, false>(p, mine, row0, warps, nb, lane);
+            }
         } else {
             for (int k = 0; k < nb; ++k) {
                 const int64_t s = __shfl_sync(0xffffffffu, mine, k);
@@ -287,6 +321,20 @@ gather_kernel(const __grid_constant__ GatherParams p) {
         }
         mine = resolve_batch(p, row0 + 32 * warps, warps, n_rows, lane);
     }
+}
+
+// The default instance (every launch the grouped copy and the many-plane small-row
+// instance do not take) keeps at most 88 registers, so two of its blocks and one
+// 512-thread lookup block (40 registers) share an SM in the decode step's
+// concurrent form; the many-plane small-row instance runs alone and may use the
+// 128 registers of two blocks per SM.
+__global__ void __maxnreg__(88) gather_kernel(const __grid_constant__ GatherParams p) {
+    gather_body<kUnroll, false>(p);
+}
+
+__global__ void __launch_bounds__(kGatherThreads, kGatherBlocksPerSM)
+gather_small_rows_kernel(const __grid_constant__ GatherParams p) {
+    gather_body<kSmallUnroll, true>(p);
 }
 
 // Rows of G = row_bytes / 16 vectors per plane, G a power of two of at most 32
@@ -375,8 +423,13 @@ gather_grouped_kernel(const __grid_constant__ GatherParams p) {
 // planes take the grouped copy (0 = never); the many-plane grouped instance keeps
 // EKV_GATHER_MANY_RG row groups x EKV_GATHER_MANY_PL planes in flight; with
 // EKV_GATHER_HONOR_READY 0 the indices-ready flag is ignored.
+// Measured on B200: the grouped copy takes config 4's per-layer two-plane launches
+// at the TP8 shard from 0.660 to 0.527 ms per 48-layer step (one shared output pair),
+// but over all 72 planes of a config-2 launch it trails the flattened copy (0.864 vs
+// 0.914 of the copy peak at 256 B rows, 0.896 vs 0.930 at 512 B), so only few-plane
+// launches take it.
 #ifndef EKV_GATHER_GROUPED_MAX_PLANES
-#define EKV_GATHER_GROUPED_MAX_PLANES 256
+#define EKV_GATHER_GROUPED_MAX_PLANES 4
 #endif
 #ifndef EKV_GATHER_MANY_RG
 #define EKV_GATHER_MANY_RG 2
@@ -392,7 +445,8 @@ using GatherKernel = void (*)(GatherParams);
 
 // The kernel instance for `n_planes` planes of `row_bytes` rows; `slot` names
 // it in the per-device grid cache.
-GatherKernel gather_kernel_for(const GatherParams& p, int& slot) {
+GatherKernel gather_kernel_for(const GatherParams& p, int& slot, size_t& smem) {
+    smem = 0;
     if (p.n_planes <= EKV_GATHER_GROUPED_MAX_PLANES && p.plane_or % 16 == 0 && p.vec_shift >= 0 &&
         p.vec_shift <= 5) {
         if (p.n_planes <= 2) {
@@ -409,14 +463,19 @@ GatherKernel gather_kernel_for(const GatherParams& p, int& slot) {
     const bool small = kSmallRowBytes > 0 && p.row_bytes <= kSmallRowBytes &&
                        static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) > kFlatRowLimit;
     slot = small ? 1 : 0;
-    return small ? gather_kernel<kSmallUnroll, true> : gather_kernel<kUnroll, false>;
+    return small ? gather_small_rows_kernel : gather_kernel;
 }
 
-int gather_grid(GatherKernel kernel, int slot, int device, int64_t n_rows) {
+int gather_grid(GatherKernel kernel, int slot, size_t smem, int device, int64_t n_rows) {
     static std::atomic<int> cached[5][64];  // per instance and device; a race computes twice
     int grid = device < 64 ? cached[slot][device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
-        grid = persistent_grid(reinterpret_cast<const void*>(kernel), kGatherThreads, 0, device);
+        if (smem > 48 * 1024) {
+            cuda_check(cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
+                       "configure gather shared memory");
+        }
+        grid = persistent_grid(reinterpret_cast<const void*>(kernel), kGatherThreads, smem, device);
         if (device < 64) cached[slot][device].store(grid, std::memory_order_relaxed);
     }
     const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
@@ -495,9 +554,10 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         const int64_t n_rows = batch * selected;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         int slot = 0;
-        const GatherKernel kernel = gather_kernel_for(p, slot);
-        launch_dependent(kernel, dim3(gather_grid(kernel, slot, device, n_rows)), dim3(kGatherThreads), 0, s,
-                         "gather_rows launch", p);
+        size_t smem = 0;
+        const GatherKernel kernel = gather_kernel_for(p, slot, smem);
+        launch_dependent(kernel, dim3(gather_grid(kernel, slot, smem, device, n_rows)), dim3(kGatherThreads), smem,
+                         s, "gather_rows launch", p);
         check_launch("gather_rows launch");
     });
 }

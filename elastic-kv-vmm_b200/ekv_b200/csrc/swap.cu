@@ -18,7 +18,8 @@
 //                the layer, from host history (pinned memory read through
 //                unified addressing, or device memory) into its new hot slot of
 //                the fixed-position hot pool (sink chunk, then one region per
-//                request); tasks beyond a request's miss count are skipped.
+//                request), many rows in flight per warp; tasks beyond a
+//                request's miss count are skipped.
 //
 // Victim choice (clock order, hits pinned) is this build's policy; the
 // reference's LRU lives in third-party code that is not part of the reference.
@@ -174,13 +175,28 @@ __device__ __forceinline__ void warp_move(const char* src, char* dst, int64_t by
     }
 }
 
-// A fixed grid of EKV_PROMOTE_BLOCKS_PER_SM blocks per SM (8 warps each), one
-// 2 KiB row in flight per warp, leaves the SMs' other slots (registers: 2
-// gather blocks + 1 promote block fit) to a gather kernel running concurrently
-// on another stream.  Warps walk each request's miss list directly
-// (per_request warps share one request), so no time goes to the columns that
-// hit.
-__global__ void __launch_bounds__(kPromoteThreads)
+#ifndef EKV_PROMOTE_UNROLL
+#define EKV_PROMOTE_UNROLL 4  // 16-byte vectors in flight per lane
+#endif
+#ifndef EKV_PROMOTE_MAX_REGISTERS
+#define EKV_PROMOTE_MAX_REGISTERS 72  // no spills at 4 in flight
+#endif
+constexpr int kPromoteUnroll = EKV_PROMOTE_UNROLL;
+
+// Each of a request's warps takes an equal contiguous share of its misses (so no
+// time goes to the columns that hit), 32 at a time: one per lane, its history row
+// and hot slot resolved once.  The warp then streams the flattened (miss, plane,
+// vector) items with kPromoteUnroll 16-byte loads in flight per lane before storing
+// them.  The reads cross the host link from pinned memory, so the bytes in flight
+// bound the copy: a warp that moved one row at a time kept one 256 B row in flight
+// at the TP8 shard (33 GB/s); this keeps up to 32 x 4 x 16 B and measured 40 GB/s
+// (config 5 at the TP8 shard, 15.5 -> 12.8 ms per step; equal at 2 KiB rows).  A
+// fixed grid of EKV_PROMOTE_BLOCKS_PER_SM blocks per SM (8 warps each) at most
+// EKV_PROMOTE_MAX_REGISTERS registers leaves room on every SM for two gather blocks
+// of 88 registers, so the swap pipeline runs layer i's gather during layer i+1's
+// promotion (6 loads in flight under an 80-register cap spilled and lost that
+// overlap: 13.9 ms; a 64-register cap: 14.5 ms).
+__global__ void __maxnreg__(EKV_PROMOTE_MAX_REGISTERS)
 promote_kernel(const __grid_constant__ PromoteParams p) {
     grid_dependency_wait();
     allow_dependents();
@@ -191,25 +207,70 @@ promote_kernel(const __grid_constant__ PromoteParams p) {
     const int64_t request_stride = warps / per_request;
     if (w >= per_request * request_stride) return;  // the remainder: every request is covered without it
     const int64_t sub = w % per_request;
-    const int64_t align = alignment_of(p.addr_or | static_cast<uint64_t>(p.row_bytes));
+    // 16-byte items need aligned addresses and a vector index that fits the item key.
+    const bool vec16 = alignment_of(p.addr_or | static_cast<uint64_t>(p.row_bytes)) == 16 &&
+                       p.row_bytes <= (int64_t{1} << 20);
+    const uint32_t vecs = static_cast<uint32_t>(p.row_bytes >> 4);
+    const uint32_t per_miss = static_cast<uint32_t>(p.n_planes) * vecs;
     for (int64_t b = w / per_request; b < p.batch; b += request_stride) {
         const int64_t count = min(static_cast<int64_t>(p.miss_count[b]), p.k);
-        for (int64_t r = sub; r < count; r += per_request) {
-            const int32_t slot = p.promo_slot[b * p.promo_row + r];
-            const int32_t token = p.miss_list[b * p.list_row + r];
-            // A slot outside the request's hot region (or a token outside its history)
-            // is skipped: the copy never leaves the buffers it was given.
-            if (slot < 0 || token < 0 || token >= p.history_rows_per_request ||
-                (static_cast<int64_t>(slot) + 1) * p.row_bytes > p.request_bytes) {
-                continue;
+        const int64_t share = (count + per_request - 1) / per_request;
+        const int64_t first = sub * share;
+        const int64_t last = min(first + share, count);
+        for (int64_t r0 = first; r0 < last; r0 += 32) {
+            const int64_t r = r0 + lane;
+            int64_t src = -1, dst = 0;
+            if (r < last) {
+                const int32_t slot = p.promo_slot[b * p.promo_row + r];
+                const int32_t token = p.miss_list[b * p.list_row + r];
+                // A slot outside the request's hot region (or a token outside its history)
+                // is skipped: the copy never leaves the buffers it was given.
+                if (slot >= 0 && token >= 0 && token < p.history_rows_per_request &&
+                    (static_cast<int64_t>(slot) + 1) * p.row_bytes <= p.request_bytes) {
+                    src = (b * p.history_rows_per_request + token) * p.row_bytes;
+                    dst = p.sink_bytes + b * p.request_bytes + static_cast<int64_t>(slot) * p.row_bytes;
+                }
             }
-            const int64_t src_row = (b * p.history_rows_per_request + token) * p.row_bytes;
-            const int64_t dst_row = p.sink_bytes + b * p.request_bytes + static_cast<int64_t>(slot) * p.row_bytes;
-            for (int plane = 0; plane < p.n_planes; ++plane) {
-                if (align == 16) {
-                    warp_move<uint4>(p.history[plane] + src_row, p.hot[plane] + dst_row, p.row_bytes, lane);
-                } else {
-                    warp_move<uint8_t>(p.history[plane] + src_row, p.hot[plane] + dst_row, p.row_bytes, lane);
+            const int nb = static_cast<int>(last - r0 < 32 ? last - r0 : 32);
+            if (vec16) {
+                // Item key: miss (5 bits) | plane (8 bits) | vector (16 bits), all ones = no copy.
+                const uint32_t total = static_cast<uint32_t>(nb) * per_miss;
+                for (uint32_t base = 0; base < total; base += 32 * kPromoteUnroll) {
+                    uint4 v[kPromoteUnroll];
+                    uint32_t key[kPromoteUnroll];
+#pragma unroll
+                    for (int u = 0; u < kPromoteUnroll; ++u) {
+                        const uint32_t idx = base + u * 32 + lane;
+                        const uint32_t m = idx < total ? idx / per_miss : 0;
+                        const uint32_t rem = idx - m * per_miss;
+                        const uint32_t plane = rem / vecs;
+                        const uint32_t vec = rem - plane * vecs;
+                        const int64_t s = __shfl_sync(0xffffffffu, src, static_cast<int>(m));
+                        key[u] = (idx < total && s >= 0) ? (m << 24) | (plane << 16) | vec : ~0u;
+                        if (key[u] != ~0u) {
+                            v[u] = *reinterpret_cast<const uint4*>(p.history[plane] + s +
+                                                                   (static_cast<int64_t>(vec) << 4));
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < kPromoteUnroll; ++u) {
+                        const int m = key[u] == ~0u ? 0 : static_cast<int>(key[u] >> 24);
+                        const int64_t d = __shfl_sync(0xffffffffu, dst, m);
+                        if (key[u] != ~0u) {
+                            const uint32_t plane = (key[u] >> 16) & 0xffu;
+                            const int64_t vec = key[u] & 0xffffu;
+                            *reinterpret_cast<uint4*>(p.hot[plane] + d + (vec << 4)) = v[u];
+                        }
+                    }
+                }
+            } else {
+                for (int k = 0; k < nb; ++k) {
+                    const int64_t s = __shfl_sync(0xffffffffu, src, k);
+                    const int64_t d = __shfl_sync(0xffffffffu, dst, k);
+                    if (s < 0) continue;
+                    for (int plane = 0; plane < p.n_planes; ++plane) {
+                        warp_move<uint8_t>(p.history[plane] + s, p.hot[plane] + d, p.row_bytes, lane);
+                    }
                 }
             }
         }
