@@ -1171,9 +1171,9 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     AND kernel) -- the combine that replaces the reference's pickled all_gather_object
     and rank_demotions intersection (scheduler_budget.py:1447-1452,
     runtime_value.py:167-214).  The layers' launches are replayed from one CUDA
-    graph; the bitmap build and the combine, which depend on chunk ownership only,
-    run eagerly on a second stream beside them, inside the timed step (the
-    sequential form, combine after the layers, is timed too).  Reported: each
+    graph; the bitmap build and the combine run eagerly after them, inside the
+    timed step (the form with the combine on a second stream beside the layers is
+    timed too).  Reported: each
     layer's lookup beside its mapped gather (the gather reads
     slots from the residency map, not from the lookup); timed beside it: the plain
     layer order (lookup, then the direct gather of its slots) and the pipelined order
@@ -1313,10 +1313,12 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
         build_bitmap()
         joint["bits"] = combine_freeable(bits_buf)
 
-    def step(mode, overlap=True):
-        # The freeable bitmap and its cross-rank AND depend only on chunk ownership, not
-        # on the layers' rows: they run on a second stream beside the layers' launches
-        # and the step ends when both are done.  overlap=False runs them after the layers.
+    def step(mode, overlap=False):
+        # The freeable bitmap and its cross-rank AND run after the layers.  They depend only
+        # on chunk ownership, so overlap=True runs them on a second stream beside the layers
+        # instead -- measured slower across ranks: the gathers' persistent grids hold every
+        # SM, so the NCCL kernels, which wait for the peer rank's, start late (2 GPUs: +334 us
+        # per step against +30 us after the layers).
         if not overlap:
             replay(mode)
             bitmap_and_combine()
@@ -1331,7 +1333,7 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     with ClockSampler(dist.local_rank) as clocks:
         for mode in modes:
             mode_ms[mode] = timed(lambda: step(mode), steps, warmup, dist) / steps
-        sequential_ms = timed(lambda: step("concurrent", overlap=False), steps, warmup, dist) / steps
+        overlapped_ms = timed(lambda: step("concurrent", overlap=True), steps, warmup, dist) / steps
         without_combine_ms = timed(lambda: replay("concurrent"), steps, warmup, dist) / steps
         combine_alone_ms = timed(bitmap_and_combine, steps, warmup, dist) / steps
     torch.cuda.synchronize()
@@ -1379,12 +1381,12 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
                              "bytes = hit rows x 4 x row_bytes (K and V read and written) + miss rows x 2 x "
                              "row_bytes (zero rows written) + 13 B per lookup + 4 B per miss-list entry"},
         "combine": {"what": ("freeable-bitmap build (counts + bitmap kernels) and NCCL all_gather_into_tensor "
-                             "of each rank's 512 B bitmap + AND kernel, on a second stream beside the layers"
-                             if dist.world > 1 else "freeable-bitmap build, single rank (no exchange)"),
+                             "of each rank's 512 B bitmap + AND kernel, after the layers"
+                             if dist.world > 1 else "freeable-bitmap build after the layers, single rank (no exchange)"),
                     "alone_us": combine_alone_ms * 1e3,
                     "us_added_to_step": (ms_per_step - without_combine_ms) * 1e3,
                     "step_without_combine_ms": without_combine_ms,
-                    "step_with_combine_after_layers_ms": sequential_ms,
+                    "step_with_combine_on_second_stream_ms": overlapped_ms,
                     "freeable_joint": len(bitmap_to_chunks(joint["bits"])),
                     "joint_matches_intersection": bool(joint_ok)},
         "parity_layer0_and_last": bool(parity),
