@@ -16,8 +16,10 @@ from conftest import ROOT
 
 def test_reference_arm_prints_one_json_line():
     env = {**os.environ, "CUDA_VISIBLE_DEVICES": ""}
+    # Two layers keep the CPU suite fast; the driver's run covers all 36.
     done = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
-                           "--warmup", "1"], capture_output=True, text=True, timeout=600, env=env, cwd=ROOT)
+                           "--warmup", "1", "--layers", "2"], capture_output=True, text=True, timeout=600, env=env,
+                          cwd=ROOT)
     assert done.returncode == 0, done.stderr[-2000:]
     lines = [line for line in done.stdout.splitlines() if line.strip()]
     assert len(lines) == 1, done.stdout[-2000:]
@@ -29,6 +31,7 @@ def test_reference_arm_prints_one_json_line():
     assert result["e2e"]["h2d_bytes_per_step"] == 0 and result["e2e"]["d2h_bytes_per_step"] == 0
     assert result["cpu_baseline"]["kind"] in ("port", "reference") and result["cpu_baseline"]["cores"] >= 1
     assert "workload" in result["config"]
+    assert result["config"]["layers"] == 2 and result["config"]["layers_sampled"] == 2
 
 
 def test_reference_arm_other_ranks_exit_quietly():
