@@ -1174,19 +1174,21 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     AND kernel) -- the combine that replaces the reference's pickled all_gather_object
     and rank_demotions intersection (scheduler_budget.py:1447-1452,
     runtime_value.py:167-214).  The layers' launches are replayed from one CUDA
-    graph; the bitmap build and the combine run eagerly after them, inside the
-    timed step (the form with the combine on a second stream beside the layers is
-    timed too).  Reported: each
-    layer's lookup beside its mapped gather (the gather reads
-    slots from the residency map, not from the lookup); timed beside it: the plain
-    layer order (lookup, then the direct gather of its slots) and the pipelined order
-    (layer i's gather beside layer i+1's lookup, which needs every Top-K up front)."""
+    graph; the bitmap build runs eagerly on a second stream beside them and the
+    exchange + AND after them, inside the timed step (build and exchange after the
+    layers, and both beside them, are timed too).  Reported: each layer's lookup
+    beside its mapped gather (the gather reads slots from the residency map, not from
+    the lookup), which holds when layer i's Top-K is known only after layer i-1; timed
+    beside it: the plain layer order (lookup, then the direct gather of its slots), and
+    two forms that need every layer's Top-K up front -- the pipelined order (layer i's
+    gather beside layer i+1's lookup) and the multi-layer form (one lookup launch over
+    all layers, then one ekv_gather_layers launch)."""
     import numpy as np
 
     from ekv_b200.pipeline import LayerPipeline
     from ekv_b200.releasable import bitmap_to_chunks, combine_freeable, freeable_bitmap
     from ekv_b200.resident_lookup import LookupPlan
-    from ekv_b200.sparse_read import PlaneGather
+    from ekv_b200.sparse_read import LayerGather, PlaneGather
     from ekv_b200.virtual_layout import VirtualKVLayout
     from oracle import gather as og
     from oracle import lookup as ol
@@ -1202,10 +1204,14 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     plane_elems = layout.capacity_bytes // 2
     gen = torch.Generator(device=dev).manual_seed(4)
     n_hits = int(k * c["hit_fraction"])
+    # Every layer's residency map and Top-K are slices of one stacked tensor, so the
+    # multi-layer form can look all layers up in one launch over layers x requests rows.
+    maps_all = torch.full((layers, reqs, ctx), -1, dtype=torch.int32, device=dev)
+    topks_all = torch.empty((layers, reqs, k), dtype=torch.int32, device=dev)
     maps, topks, planes, outs = [], [], [], []
-    for _ in range(layers):
-        res_map = torch.full((reqs, ctx), -1, dtype=torch.int32, device=dev)
-        topk = torch.empty((reqs, k), dtype=torch.int32, device=dev)
+    for layer in range(layers):
+        res_map = maps_all[layer]
+        topk = topks_all[layer]
         for r in range(reqs):
             perm = torch.randperm(ctx, generator=gen, device=dev)
             res_map[r, perm[:hot]] = torch.randperm(hot, generator=gen, device=dev).to(torch.int32)
@@ -1240,7 +1246,23 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
               for layer in range(layers)]
     pipelines = {"concurrent": LayerPipeline(lookups, mapped, dev, wait=False),
                  "pipelined": LayerPipeline(lookups, gathers, dev)}
-    modes = ("order", "concurrent", "pipelined")
+    # Every layer's Top-K known when the step starts: one lookup launch over all layers'
+    # rows (the stacked maps and Top-K as layers x requests rows), then every layer's
+    # direct K,V gather of its slots in one ekv_gather_layers launch.  Each residency-map
+    # entry is read once per step (the mapped forms read it in the lookup and again in the
+    # gather), and no launch boundary separates the layers.
+    all_lookup = LookupPlan(maps_all.view(layers * reqs, ctx), topks_all.view(layers * reqs, k))
+    all_slots = all_lookup.slots.view(layers, reqs, k)
+    layer_gather = LayerGather(planes, [all_slots[layer] for layer in range(layers)], req_ids, lengths, None, None,
+                               outs, layout, planes_per_layer=2, indirect=False)
+
+    def multi_layer_step():
+        all_lookup()
+        layer_gather()
+
+    pipelines["multi_layer"] = multi_layer_step
+    pipelines["multi_layer_gather"] = layer_gather  # the gather launch alone: its kernel's roofline
+    modes = ("order", "concurrent", "pipelined", "multi_layer")
     projection, refs, mapped_bits, candidate, unmapped, n_chunks, _ = freeable_world(dist, shard)
     counts_buf = projection.counts(candidate)
     bits_buf = freeable_bitmap(counts_buf, refs, mapped_bits)
@@ -1274,25 +1296,28 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     check = sorted({0, layers // 2, layers - 1})
     plain_out = [outs[2 * layer + w].clone() for layer in check for w in range(2)]
     plain_lookup = [t.clone() for t in (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count)]
+    last_of_all = (all_slots[-1], all_lookup.miss_list.view(layers, reqs, k)[-1],
+                   all_lookup.miss_count.view(layers, reqs)[-1])
     for mode in modes[1:]:
-        for t in (*outs, lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count):
+        last_lookup = last_of_all if mode == "multi_layer" else \
+            (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count)
+        for t in (*outs, *last_lookup):
             t.zero_()
         layers_step(mode)
         torch.cuda.synchronize()
         parity &= all(torch.equal(outs[2 * layer + w], plain_out[2 * i + w])
                       for i, layer in enumerate(check) for w in range(2))
-        parity &= all(torch.equal(a, b) for a, b in zip(
-            (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count), plain_lookup))
+        parity &= all(torch.equal(a, b) for a, b in zip(last_lookup, plain_lookup))
     del plain_out, plain_lookup
     graphs = {}
     try:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
-            for mode in modes:
+            for mode in (*modes, "multi_layer_gather"):
                 layers_step(mode)
         torch.cuda.current_stream(dev).wait_stream(side)
-        for mode in modes:
+        for mode in (*modes, "multi_layer_gather"):
             graphs[mode] = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graphs[mode]):
                 layers_step(mode)
@@ -1316,29 +1341,37 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
         build_bitmap()
         joint["bits"] = combine_freeable(bits_buf)
 
-    def step(mode, overlap=False):
-        # The freeable bitmap and its cross-rank AND run after the layers.  They depend only
-        # on chunk ownership, so overlap=True runs them on a second stream beside the layers
-        # instead -- measured slower across ranks: the gathers' persistent grids hold every
-        # SM, so the NCCL kernels, which wait for the peer rank's, start late (2 GPUs: +334 us
-        # per step against +30 us after the layers).
-        if not overlap:
+    def step(mode, combine="beside"):
+        # The freeable bitmap depends only on chunk ownership.  "beside" (reported): its
+        # build runs on a second stream beside the layers and the cross-rank exchange + AND
+        # after them.  "after": build and exchange after the layers.  "second_stream": build
+        # and exchange beside the layers -- measured slower across ranks: the gathers'
+        # persistent grids hold every SM, so the NCCL kernels, which wait for the peer
+        # rank's, start late (2 GPUs: +334 us per step against +30 us after the layers).
+        if combine == "after":
             replay(mode)
             bitmap_and_combine()
             return
         bitmap_stream.wait_stream(main_stream)
         with torch.cuda.stream(bitmap_stream):
-            bitmap_and_combine()
+            if combine == "second_stream":
+                bitmap_and_combine()
+            else:
+                build_bitmap()
         replay(mode)
         main_stream.wait_stream(bitmap_stream)
+        if combine == "beside":
+            joint["bits"] = combine_freeable(bits_buf)
 
     mode_ms = {}
     with ClockSampler(dist.local_rank) as clocks:
         for mode in modes:
             mode_ms[mode] = timed(lambda: step(mode), steps, warmup, dist) / steps
-        overlapped_ms = timed(lambda: step("concurrent", overlap=True), steps, warmup, dist) / steps
+        after_ms = timed(lambda: step("concurrent", combine="after"), steps, warmup, dist) / steps
+        second_stream_ms = timed(lambda: step("concurrent", combine="second_stream"), steps, warmup, dist) / steps
         without_combine_ms = timed(lambda: replay("concurrent"), steps, warmup, dist) / steps
         combine_alone_ms = timed(bitmap_and_combine, steps, warmup, dist) / steps
+        layer_gather_ms = timed(lambda: replay("multi_layer_gather"), steps, warmup, dist) / steps
     torch.cuda.synchronize()
     expected_joint = bitmap_to_chunks(bits_buf)
     for r in range(dist.world):
@@ -1350,7 +1383,8 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     misses = units - hits
     # K and V: a hit row is read and written, a miss row written as zeros; lookup: 13 B per
     # Top-K id (index, map entry, slot, mask) + 4 B per miss-list entry.
-    bytes_per_step = hits * 4 * row_bytes + misses * 2 * row_bytes + units * (4 + 4 + 4 + 1) + misses * 4
+    gather_bytes = hits * 4 * row_bytes + misses * 2 * row_bytes
+    bytes_per_step = gather_bytes + units * (4 + 4 + 4 + 1) + misses * 4
     peak, peak_source = measured_hbm_peak()
     achieved = bytes_per_step / (ms_per_step / 1e3) / 1e9
     result = {
@@ -1376,20 +1410,33 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
                                     "reference's order)"},
             "pipelined": {"ms_per_step": mode_ms["pipelined"], "value": units / (mode_ms["pipelined"] / 1e3),
                           "what": "layer i's direct gather on a second stream while layer i+1's lookup runs; "
-                                  "valid only when every layer's Top-K is known when the step starts"}},
+                                  "valid only when every layer's Top-K is known when the step starts"},
+            "multi_layer": {"ms_per_step": mode_ms["multi_layer"],
+                            "value": units / (mode_ms["multi_layer"] / 1e3),
+                            "frac": bytes_per_step / (mode_ms["multi_layer"] / 1e3) / 1e9 / peak,
+                            "gather_launch_us": layer_gather_ms * 1e3,
+                            "gather_launch_frac": gather_bytes / (layer_gather_ms / 1e3) / 1e9 / peak,
+                            "what": "one lookup launch over every layer's rows, then every layer's direct K,V "
+                                    "gather of its slots in one ekv_gather_layers launch (no launch boundary "
+                                    "between layers, each residency-map entry read once); valid only when "
+                                    "every layer's Top-K is known when the step starts.  gather_launch_*: "
+                                    "that gather launch alone against its own bytes"}},
         "hbm_gbs_per_gpu": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_source,
                      "note": f"step = {layers} lookups + {layers} two-plane gathers + bitmap build + combine; "
                              "bytes = hit rows x 4 x row_bytes (K and V read and written) + miss rows x 2 x "
                              "row_bytes (zero rows written) + 13 B per lookup + 4 B per miss-list entry"},
-        "combine": {"what": ("freeable-bitmap build (counts + bitmap kernels) and NCCL all_gather_into_tensor "
-                             "of each rank's 512 B bitmap + AND kernel, after the layers"
-                             if dist.world > 1 else "freeable-bitmap build after the layers, single rank (no exchange)"),
+        "combine": {"what": ("freeable-bitmap build (counts + bitmap kernels) on a second stream beside the "
+                             "layers, then NCCL all_gather_into_tensor of each rank's 512 B bitmap + AND kernel "
+                             "after them"
+                             if dist.world > 1 else "freeable-bitmap build (counts + bitmap kernels) on a second "
+                                                    "stream beside the layers, single rank (no exchange)"),
                     "alone_us": combine_alone_ms * 1e3,
                     "us_added_to_step": (ms_per_step - without_combine_ms) * 1e3,
                     "step_without_combine_ms": without_combine_ms,
-                    "step_with_combine_on_second_stream_ms": overlapped_ms,
+                    "step_with_build_and_exchange_after_the_layers_ms": after_ms,
+                    "step_with_combine_on_second_stream_ms": second_stream_ms,
                     "freeable_joint": len(bitmap_to_chunks(joint["bits"])),
                     "joint_matches_intersection": bool(joint_ok)},
         "parity_layer0_and_last": bool(parity),

@@ -15,6 +15,7 @@ import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "lib" / "libekv_b200.so"
 MAX_PLANES = 256  # EKV_MAX_PLANES
+MAX_LAYERS = 128  # EKV_MAX_LAYERS
 SHARED_INLINE_MAX = 512  # EKV_SHARED_INLINE_MAX
 SHADOW_MAX_LAYERS = 128  # EKV_SHADOW_MAX_LAYERS
 
@@ -56,6 +57,12 @@ _KERNELS = {
     "ekv_gather_rows_planes": [
         _u64p, _u64p, _i32, _i64,
         _p, _i32, _p, _i32, _p, _i32, _p, _i32, _p, _i32,
+        _i64, _i64, _i64, _i64, _i64, _i64,
+        _i32, _i32, _p,
+    ],
+    "ekv_gather_layers": [
+        _u64p, _u64p, _i32, _i32, _i64,
+        _u64p, _i32, _p, _i32, _p, _i32, _u64p, _i32, _p, _i32,
         _i64, _i64, _i64, _i64, _i64, _i64,
         _i32, _i32, _p,
     ],

@@ -95,22 +95,25 @@ constexpr int kUnroll = EKV_GATHER_UNROLL;
 constexpr int64_t kSmallRowBytes = EKV_GATHER_SMALL_ROW_BYTES;
 constexpr int kSmallUnroll = EKV_GATHER_SMALL_UNROLL;
 
-// Byte offset of row r inside every source plane, or valid = false.
-__device__ __forceinline__ int64_t resolve_row(const GatherParams& p, int64_t r, bool& valid) {
+// Byte offset of row r inside every source plane, or valid = false.  `positions`
+// and `table` stand in for p.positions and p.request_table (one layer's of a
+// multi-layer launch).
+__device__ __forceinline__ int64_t resolve_row_at(const GatherParams& p, const void* positions,
+                                                  const void* table, int64_t r, bool& valid) {
     const int64_t b = r / p.selected;
-    const int64_t pos = load_index(p.positions, p.pos_es, r);
+    const int64_t pos = load_index(positions, p.pos_es, r);
     const int64_t length = load_index(p.lengths, p.len_es, b);
     valid = pos >= 0 && pos < length;
     if (!valid) return 0;
     const int64_t req = load_index(p.request_ids, p.req_es, b);
     int64_t element;
     if (p.indirect == 1) {
-        const int64_t logical = load_index(p.request_table, p.table_es, req * p.table_width + pos);
+        const int64_t logical = load_index(table, p.table_es, req * p.table_width + pos);
         element = load_index(p.slot_offsets, p.off_es, logical);
     } else if (p.indirect == 2) {
         // Mapped: the table holds the row's slot in the request's fixed region, -1 if
         // absent; a slot past the region reads as absent too (never outside the region).
-        const int64_t slot = load_index(p.request_table, p.table_es, req * p.table_width + pos);
+        const int64_t slot = load_index(table, p.table_es, req * p.table_width + pos);
         if (slot < 0 || (slot + 1) * p.width > p.request_stride) {
             valid = false;
             return 0;
@@ -142,10 +145,11 @@ __device__ __forceinline__ void store_vec(uint4* dst, uint4 value) {
 #endif
 }
 
+// Per-row copies: planes plane0 .. plane0 + n_planes - 1.
 __device__ __forceinline__ void copy_row_vec16(const GatherParams& p, bool valid, int64_t src_off,
-                                               int64_t dst_off, unsigned lane) {
+                                               int64_t dst_off, unsigned lane, int plane0, int n_planes) {
     const int64_t vecs = p.row_bytes >> 4;
-    const int64_t total = static_cast<int64_t>(p.n_planes) * vecs;
+    const int64_t total = static_cast<int64_t>(n_planes) * vecs;
     for (int64_t base = 0; base < total; base += 32 * kUnroll) {
         uint4 v[kUnroll];
 #pragma unroll
@@ -155,7 +159,7 @@ __device__ __forceinline__ void copy_row_vec16(const GatherParams& p, bool valid
             if (valid && idx < total) {
                 const int64_t plane = p.vec_shift >= 0 ? (idx >> p.vec_shift) : idx / vecs;
                 const int64_t vec = idx - plane * vecs;
-                v[u] = load_vec(reinterpret_cast<const uint4*>(p.src[plane] + src_off) + vec);
+                v[u] = load_vec(reinterpret_cast<const uint4*>(p.src[plane0 + plane] + src_off) + vec);
             }
         }
 #pragma unroll
@@ -164,7 +168,7 @@ __device__ __forceinline__ void copy_row_vec16(const GatherParams& p, bool valid
             if (idx < total) {
                 const int64_t plane = p.vec_shift >= 0 ? (idx >> p.vec_shift) : idx / vecs;
                 const int64_t vec = idx - plane * vecs;
-                store_vec(reinterpret_cast<uint4*>(p.dst[plane] + dst_off) + vec, v[u]);
+                store_vec(reinterpret_cast<uint4*>(p.dst[plane0 + plane] + dst_off) + vec, v[u]);
             }
         }
     }
@@ -172,29 +176,29 @@ __device__ __forceinline__ void copy_row_vec16(const GatherParams& p, bool valid
 
 template <typename T>
 __device__ __forceinline__ void copy_row_elems(const GatherParams& p, bool valid, int64_t src_off,
-                                               int64_t dst_off, unsigned lane) {
+                                               int64_t dst_off, unsigned lane, int plane0, int n_planes) {
     const int64_t elems = p.row_bytes / static_cast<int64_t>(sizeof(T));
-    const int64_t total = static_cast<int64_t>(p.n_planes) * elems;
+    const int64_t total = static_cast<int64_t>(n_planes) * elems;
     for (int64_t idx = lane; idx < total; idx += 32) {
         const int64_t plane = idx / elems;
         const int64_t e = idx - plane * elems;
         T value = T(0);
-        if (valid) value = reinterpret_cast<const T*>(p.src[plane] + src_off)[e];
-        reinterpret_cast<T*>(p.dst[plane] + dst_off)[e] = value;
+        if (valid) value = reinterpret_cast<const T*>(p.src[plane0 + plane] + src_off)[e];
+        reinterpret_cast<T*>(p.dst[plane0 + plane] + dst_off)[e] = value;
     }
 }
 
 // Warp-cooperative copy of one row out of every plane, any alignment.
 __device__ __forceinline__ void copy_row_any(const GatherParams& p, bool valid, int64_t src_off,
-                                             int64_t dst_off, unsigned lane) {
+                                             int64_t dst_off, unsigned lane, int plane0, int n_planes) {
     const int64_t align = alignment_of(p.plane_or | static_cast<uint64_t>(src_off) |
                                        static_cast<uint64_t>(dst_off) | static_cast<uint64_t>(p.row_bytes));
     switch (align) {
-        case 16: copy_row_vec16(p, valid, src_off, dst_off, lane); break;
-        case 8: copy_row_elems<uint64_t>(p, valid, src_off, dst_off, lane); break;
-        case 4: copy_row_elems<uint32_t>(p, valid, src_off, dst_off, lane); break;
-        case 2: copy_row_elems<uint16_t>(p, valid, src_off, dst_off, lane); break;
-        default: copy_row_elems<uint8_t>(p, valid, src_off, dst_off, lane); break;
+        case 16: copy_row_vec16(p, valid, src_off, dst_off, lane, plane0, n_planes); break;
+        case 8: copy_row_elems<uint64_t>(p, valid, src_off, dst_off, lane, plane0, n_planes); break;
+        case 4: copy_row_elems<uint32_t>(p, valid, src_off, dst_off, lane, plane0, n_planes); break;
+        case 2: copy_row_elems<uint16_t>(p, valid, src_off, dst_off, lane, plane0, n_planes); break;
+        default: copy_row_elems<uint8_t>(p, valid, src_off, dst_off, lane, plane0, n_planes); break;
     }
 }
 
@@ -211,11 +215,13 @@ constexpr uint32_t kFlatRowLimit = EKV_GATHER_FLAT_LIMIT;  // vectors per row (a
 // belongs to row idx / per_row of the batch; with kWalk a lane's next item is 32
 // further on, so (row, remainder) advance with one compare instead of a division
 // per item.
+// Planes plane0 .. plane0 + n_planes - 1 of p.src / p.dst are copied.
 template <int kU, bool kWalk>
 __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t mine, int64_t row0,
-                                                 int64_t warps, int nb, unsigned lane) {
+                                                 int64_t warps, int nb, unsigned lane, int plane0,
+                                                 int n_planes) {
     const uint32_t vecs = static_cast<uint32_t>(p.row_bytes >> 4);
-    const uint32_t per_row = static_cast<uint32_t>(p.n_planes) * vecs;
+    const uint32_t per_row = static_cast<uint32_t>(n_planes) * vecs;
     const uint32_t total = static_cast<uint32_t>(nb) * per_row;
     uint32_t k = 0, rem = lane;
     for (uint32_t base = 0; base < total; base += 32 * kU) {
@@ -237,7 +243,7 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
             if (live && s >= 0) {
                 const uint32_t plane = p.vec_shift >= 0 ? (rem >> p.vec_shift) : rem / vecs;
                 const uint32_t vec = rem - plane * vecs;
-                v[u] = load_vec(reinterpret_cast<const uint4*>(p.src[plane] + s) + vec);
+                v[u] = load_vec(reinterpret_cast<const uint4*>(p.src[plane0 + plane] + s) + vec);
             }
             if (kWalk) {
                 rem += 32;
@@ -253,7 +259,7 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
             if (idx < total) {
                 const uint32_t plane = p.vec_shift >= 0 ? (rem_of[u] >> p.vec_shift) : rem_of[u] / vecs;
                 const uint32_t vec = rem_of[u] - plane * vecs;
-                char* row = p.dst[plane] + (row0 + static_cast<int64_t>(row_of[u]) * warps) * p.row_bytes;
+                char* row = p.dst[plane0 + plane] + (row0 + static_cast<int64_t>(row_of[u]) * warps) * p.row_bytes;
                 store_vec(reinterpret_cast<uint4*>(row) + vec, v[u]);
             }
         }
@@ -263,13 +269,19 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
 // Offset of row row0 + lane * warps in every source plane, or -1 for a zero row
 // (invalid position, or a row past the end).  Each lane resolves one row of the
 // warp's 32-row batch, so the three dependent index loads are paid once per 32 rows.
-__device__ __forceinline__ int64_t resolve_batch(const GatherParams& p, int64_t row0, int64_t warps,
-                                                 int64_t n_rows, unsigned lane) {
+__device__ __forceinline__ int64_t resolve_batch_at(const GatherParams& p, const void* positions,
+                                                    const void* table, int64_t row0, int64_t warps,
+                                                    int64_t n_rows, unsigned lane) {
     const int64_t r = row0 + static_cast<int64_t>(lane) * warps;
     bool valid = false;
     int64_t src = 0;
-    if (r < n_rows) src = resolve_row(p, r, valid);
+    if (r < n_rows) src = resolve_row_at(p, positions, table, r, valid);
     return valid ? src : -1;
+}
+
+__device__ __forceinline__ int64_t resolve_batch(const GatherParams& p, int64_t row0, int64_t warps,
+                                                 int64_t n_rows, unsigned lane) {
+    return resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane);
 }
 
 // The first batch's index chain.  With `indices_ready` the caller has promised
@@ -309,14 +321,14 @@ __device__ __forceinline__ void gather_body(const GatherParams& p) {
             // The division form for the many-plane small-row instance: its walk was
             // slower (see EKV_GATHER_SMALL_WALK).
             if ((kFlatAll ? EKV_GATHER_SMALL_WALK : EKV_GATHER_WALK) && p.n_planes * (p.row_bytes >> 4) >= 32) {
-                copy_batch_vec16<kU, true>(p, mine, row0, warps, nb, lane);
+                copy_batch_vec16<kU, true>(p, mine, row0, warps, nb, lane, 0, p.n_planes);
             } else {
-                copy_batch_vec16<kU, false>(p, mine, row0, warps, nb, lane);
+                copy_batch_vec16<kU, false>(p, mine, row0, warps, nb, lane, 0, p.n_planes);
             }
         } else {
             for (int k = 0; k < nb; ++k) {
                 const int64_t s = __shfl_sync(0xffffffffu, mine, k);
-                copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane);
+                copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane, 0, p.n_planes);
             }
         }
         mine = resolve_batch(p, row0 + 32 * warps, warps, n_rows, lane);
@@ -349,13 +361,13 @@ gather_small_rows_kernel(const __grid_constant__ GatherParams p) {
 // (instances for launches over few planes put the depth into row groups).
 template <int kRG, int kPL>
 __device__ __forceinline__ void copy_batch_grouped(const GatherParams& p, int64_t mine, int64_t row0,
-                                                   int64_t warps, int nb, unsigned lane) {
+                                                   int64_t warps, int nb, unsigned lane, int plane0,
+                                                   int n_planes) {
     const int gs = p.vec_shift;
     const int rows_per_group = 32 >> gs;
     const int groups = (nb + rows_per_group - 1) / rows_per_group;
     const int sub = static_cast<int>(lane >> gs);
     const int64_t vbyte = static_cast<int64_t>(lane & ((1u << gs) - 1u)) << 4;
-    const int n_planes = p.n_planes;
     for (int g0 = 0; g0 < groups; g0 += kRG) {
         int64_t src[kRG];
         bool live[kRG];
@@ -374,7 +386,7 @@ __device__ __forceinline__ void copy_batch_grouped(const GatherParams& p, int64_
                 for (int q = 0; q < kPL; ++q) {
                     v[j][q] = make_uint4(0u, 0u, 0u, 0u);
                     if (live[j] && src[j] >= vbyte && pb + q < n_planes) {
-                        v[j][q] = load_vec(reinterpret_cast<const uint4*>(p.src[pb + q] + src[j]));
+                        v[j][q] = load_vec(reinterpret_cast<const uint4*>(p.src[plane0 + pb + q] + src[j]));
                     }
                 }
             }
@@ -385,7 +397,7 @@ __device__ __forceinline__ void copy_batch_grouped(const GatherParams& p, int64_
 #pragma unroll
                 for (int q = 0; q < kPL; ++q) {
                     if (live[j] && pb + q < n_planes) {
-                        store_vec(reinterpret_cast<uint4*>(p.dst[pb + q] + dst), v[j][q]);
+                        store_vec(reinterpret_cast<uint4*>(p.dst[plane0 + pb + q] + dst), v[j][q]);
                     }
                 }
             }
@@ -408,14 +420,80 @@ gather_grouped_kernel(const __grid_constant__ GatherParams p) {
         const int64_t left = (n_rows - row0 + warps - 1) / warps;
         const int nb = static_cast<int>(left < 32 ? left : 32);
         if (!__ballot_sync(0xffffffffu, mine >= 0 && (mine & 15))) {
-            copy_batch_grouped<kRG, kPL>(p, mine, row0, warps, nb, lane);
+            copy_batch_grouped<kRG, kPL>(p, mine, row0, warps, nb, lane, 0, p.n_planes);
         } else {  // a row of this batch starts off a 16-byte boundary
             for (int k = 0; k < nb; ++k) {
                 const int64_t s = __shfl_sync(0xffffffffu, mine, k);
-                copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane);
+                copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane, 0, p.n_planes);
             }
         }
         mine = resolve_batch(p, row0 + 32 * warps, warps, n_rows, lane);
+    }
+}
+
+// Multi-layer launch (ekv_gather_layers): layer l gathers its rows with its own
+// positions and table out of planes l * planes_per_layer ... into the matching
+// outputs; request ids, lengths, slot offsets and the row geometry are shared.
+struct LayerGatherParams {
+    GatherParams p;  // p.src / p.dst hold every layer's planes, layer-major
+    const void* positions[EKV_MAX_LAYERS];
+    const void* tables[EKV_MAX_LAYERS];
+    int n_layers;
+    int planes_per_layer;
+};
+
+// Every warp walks the layers in order and takes, in each, the rows a per-layer
+// launch of the same grid would give it (row0 + k * warps), so a layer's 32-row
+// batches are resolved and copied exactly as in the single-layer kernels -- but
+// with no launch boundary between layers: while some warps resolve layer l+1's
+// index chains, others are still copying layer l, and DRAM sees one continuous
+// stream instead of a ramp and a drain per layer.  kRG > 0: grouped copy (rows of
+// 16-512 B, at most kPL planes per layer); kRG == 0: flattened copy.  Batches
+// with a row off the 16-byte grid take the per-row copy.  At most 88 registers,
+// as the single-layer instances, so lookup blocks still fit beside two of these.
+#ifndef EKV_GATHER_LAYERS_MAXNREG
+#define EKV_GATHER_LAYERS_MAXNREG 88
+#endif
+#ifndef EKV_GATHER_LAYERS_RG
+#define EKV_GATHER_LAYERS_RG 4  // row groups in flight per lane, two planes per layer
+#endif
+template <int kRG, int kPL>
+__global__ void __maxnreg__(EKV_GATHER_LAYERS_MAXNREG)
+gather_layers_kernel(const __grid_constant__ LayerGatherParams lp) {
+    const GatherParams& p = lp.p;
+    const int64_t n_rows = p.batch * p.selected;  // per layer
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
+    const unsigned lane = lane_id();
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5);
+    const int per_layer = lp.planes_per_layer;
+    const uint32_t per_row = static_cast<uint32_t>(per_layer) * static_cast<uint32_t>(p.row_bytes >> 4);
+    const bool vectors = p.row_bytes % 16 == 0 && p.plane_or % 16 == 0 && (kRG > 0 || per_row <= kFlatRowLimit);
+    grid_dependency_wait();
+    allow_dependents();
+    for (int layer = 0; layer < lp.n_layers; ++layer) {
+        const void* positions = lp.positions[layer];
+        const void* table = lp.tables[layer];
+        const int plane0 = layer * per_layer;
+        for (int64_t row0 = first; row0 < n_rows; row0 += 32 * warps) {
+            const int64_t left = (n_rows - row0 + warps - 1) / warps;
+            const int nb = static_cast<int>(left < 32 ? left : 32);
+            const int64_t mine = resolve_batch_at(p, positions, table, row0, warps, n_rows, lane);
+            if (vectors && !__ballot_sync(0xffffffffu, mine >= 0 && (mine & 15))) {
+                if constexpr (kRG > 0) {
+                    copy_batch_grouped<kRG, kPL>(p, mine, row0, warps, nb, lane, plane0, per_layer);
+                } else if (per_row >= 32) {
+                    copy_batch_vec16<kUnroll, true>(p, mine, row0, warps, nb, lane, plane0, per_layer);
+                } else {
+                    copy_batch_vec16<kUnroll, false>(p, mine, row0, warps, nb, lane, plane0, per_layer);
+                }
+            } else {
+                for (int k = 0; k < nb; ++k) {
+                    const int64_t s = __shfl_sync(0xffffffffu, mine, k);
+                    copy_row_any(p, s >= 0, s < 0 ? 0 : s, (row0 + k * warps) * p.row_bytes, lane, plane0,
+                                 per_layer);
+                }
+            }
+        }
     }
 }
 
@@ -466,16 +544,16 @@ GatherKernel gather_kernel_for(const GatherParams& p, int& slot, size_t& smem) {
     return small ? gather_small_rows_kernel : gather_kernel;
 }
 
-int gather_grid(GatherKernel kernel, int slot, size_t smem, int device, int64_t n_rows) {
-    static std::atomic<int> cached[5][64];  // per instance and device; a race computes twice
+int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n_rows) {
+    static std::atomic<int> cached[8][64];  // per instance and device; a race computes twice
     int grid = device < 64 ? cached[slot][device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
         if (smem > 48 * 1024) {
-            cuda_check(cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+            cuda_check(cudaFuncSetAttribute(kernel,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
                        "configure gather shared memory");
         }
-        grid = persistent_grid(reinterpret_cast<const void*>(kernel), kGatherThreads, smem, device);
+        grid = persistent_grid(kernel, kGatherThreads, smem, device);
         if (device < 64) cached[slot][device].store(grid, std::memory_order_relaxed);
     }
     const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
@@ -487,6 +565,61 @@ int log2_exact(int64_t x) {
     int shift = 0;
     while ((int64_t{1} << shift) < x) ++shift;
     return shift;
+}
+
+// Checks and fields shared by the single- and multi-layer entry points (everything
+// but the planes and the per-layer index arrays).  `indirect` carries the mode and
+// the flag bits; returns the mode.
+int common_params(GatherParams& p, int64_t itemsize, int positions_esize, const void* request_ids,
+                  int request_ids_esize, const void* lengths, int lengths_esize, int table_esize,
+                  const void* slot_offsets, int offsets_esize, int64_t batch, int64_t selected, int64_t width,
+                  int64_t table_width, int64_t request_stride, int64_t sink_elements, int indirect) {
+    require(request_ids && lengths, "null index argument");
+    check_esize(positions_esize, "positions");
+    check_esize(request_ids_esize, "request_ids");
+    check_esize(lengths_esize, "lengths");
+    const int flags = indirect & ~3;
+    require(flags == 0 || flags == EKV_GATHER_INDICES_READY, "unknown gather flag bits");
+    const int mode = indirect & 3;
+    require(mode <= 2, "addressing mode must be 0 (direct), 1 (indirect) or 2 (mapped)");
+    if (mode == 1) {
+        require(slot_offsets, "indirect gather needs request_table and slot_offsets");
+        check_esize(offsets_esize, "slot_offsets");
+    }
+    if (mode) check_esize(table_esize, "request_table");
+    p.request_ids = request_ids;
+    p.lengths = lengths;
+    p.slot_offsets = slot_offsets;
+    p.batch = batch;
+    p.selected = selected;
+    p.width = width;
+    p.itemsize = itemsize;
+    p.row_bytes = width * itemsize;
+    p.table_width = table_width;
+    p.request_stride = request_stride;
+    p.sink_elements = sink_elements;
+    p.pos_es = positions_esize;
+    p.req_es = request_ids_esize;
+    p.len_es = lengths_esize;
+    p.table_es = mode ? table_esize : 8;
+    p.off_es = mode == 1 ? offsets_esize : 8;
+    p.indirect = mode;
+    p.indices_ready = EKV_GATHER_HONOR_READY ? flags != 0 : 0;
+    p.vec_shift = (p.row_bytes % 16) ? -1 : log2_exact(p.row_bytes / 16);
+    return mode;
+}
+
+void set_planes(GatherParams& p, const uint64_t* src_planes, const uint64_t* dst_planes, int n_planes) {
+    require(src_planes && dst_planes, "null plane array");
+    uint64_t plane_or = 0;
+    for (int i = 0; i < n_planes; ++i) {
+        require(src_planes[i] && dst_planes[i], "null plane address");
+        p.src[i] = reinterpret_cast<const char*>(src_planes[i]);
+        p.dst[i] = reinterpret_cast<char*>(dst_planes[i]);
+        plane_or |= src_planes[i] | dst_planes[i];
+    }
+    p.n_planes = n_planes;
+    p.plane_or = plane_or;
 }
 
 int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_planes, int64_t itemsize,
@@ -503,62 +636,80 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         if (!batch || !selected || !width) return;
         require(src_planes && dst_planes, "null plane array");
         require(positions && request_ids && lengths, "null index argument");
-        check_esize(positions_esize, "positions");
-        check_esize(request_ids_esize, "request_ids");
-        check_esize(lengths_esize, "lengths");
-        const int flags = indirect & ~3;
-        require(flags == 0 || flags == EKV_GATHER_INDICES_READY, "unknown gather flag bits");
-        const int ready = flags != 0;
-        indirect &= 3;
-        require(indirect <= 2, "addressing mode must be 0 (direct), 1 (indirect) or 2 (mapped)");
-        if (indirect == 1) {
-            require(request_table && slot_offsets, "indirect gather needs request_table and slot_offsets");
-            check_esize(table_esize, "request_table");
-            check_esize(offsets_esize, "slot_offsets");
-        } else if (indirect == 2) {
-            require(request_table, "mapped gather needs request_table (the residency map)");
-            check_esize(table_esize, "request_table");
-        }
         GatherParams p{};
+        const int mode = common_params(p, itemsize, positions_esize, request_ids, request_ids_esize, lengths,
+                                       lengths_esize, table_esize, slot_offsets, offsets_esize, batch, selected,
+                                       width, table_width, request_stride, sink_elements, indirect);
+        if (mode == 1) require(request_table, "indirect gather needs request_table and slot_offsets");
+        if (mode == 2) require(request_table, "mapped gather needs request_table (the residency map)");
         p.positions = positions;
-        p.request_ids = request_ids;
-        p.lengths = lengths;
         p.request_table = request_table;
-        p.slot_offsets = slot_offsets;
-        p.batch = batch;
-        p.selected = selected;
-        p.width = width;
-        p.itemsize = itemsize;
-        p.row_bytes = width * itemsize;
-        p.table_width = table_width;
-        p.request_stride = request_stride;
-        p.sink_elements = sink_elements;
-        p.pos_es = positions_esize;
-        p.req_es = request_ids_esize;
-        p.len_es = lengths_esize;
-        p.table_es = indirect ? table_esize : 8;
-        p.off_es = indirect == 1 ? offsets_esize : 8;
-        p.indirect = indirect;
-        p.indices_ready = EKV_GATHER_HONOR_READY ? ready : 0;
-        p.n_planes = n_planes;
-        p.vec_shift = (p.row_bytes % 16) ? -1 : log2_exact(p.row_bytes / 16);
-        uint64_t plane_or = 0;
-        for (int i = 0; i < n_planes; ++i) {
-            require(src_planes[i] && dst_planes[i], "null plane address");
-            p.src[i] = reinterpret_cast<const char*>(src_planes[i]);
-            p.dst[i] = reinterpret_cast<char*>(dst_planes[i]);
-            plane_or |= src_planes[i] | dst_planes[i];
-        }
-        p.plane_or = plane_or;
+        set_planes(p, src_planes, dst_planes, n_planes);
         bind_device(device);
         const int64_t n_rows = batch * selected;
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         int slot = 0;
         size_t smem = 0;
         const GatherKernel kernel = gather_kernel_for(p, slot, smem);
-        launch_dependent(kernel, dim3(gather_grid(kernel, slot, smem, device, n_rows)), dim3(kGatherThreads), smem,
-                         s, "gather_rows launch", p);
+        const int grid = gather_grid(reinterpret_cast<const void*>(kernel), slot, smem, device, n_rows);
+        launch_dependent(kernel, dim3(grid), dim3(kGatherThreads), smem, s, "gather_rows launch", p);
         check_launch("gather_rows launch");
+    });
+}
+
+using LayerGatherKernel = void (*)(LayerGatherParams);
+
+int gather_layers_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_layers, int planes_per_layer,
+                       int64_t itemsize, const uint64_t* positions, int positions_esize,
+                       const void* request_ids, int request_ids_esize, const void* lengths, int lengths_esize,
+                       const uint64_t* request_tables, int table_esize, const void* slot_offsets,
+                       int offsets_esize, int64_t batch, int64_t selected, int64_t width, int64_t table_width,
+                       int64_t request_stride, int64_t sink_elements, int indirect, int device, void* stream) {
+    return guarded([&] {
+        require(batch >= 0 && selected >= 0 && width >= 0, "sizes must be non-negative");
+        require(itemsize > 0, "itemsize must be positive");
+        require(n_layers >= 1 && n_layers <= EKV_MAX_LAYERS, "layer count outside [1, EKV_MAX_LAYERS]");
+        require(planes_per_layer >= 1 && static_cast<int64_t>(n_layers) * planes_per_layer <= EKV_MAX_PLANES,
+                "n_layers * planes_per_layer outside [1, EKV_MAX_PLANES]");
+        if (!batch || !selected || !width) return;
+        require(src_planes && dst_planes, "null plane array");
+        require(positions, "null positions array");
+        LayerGatherParams lp{};
+        GatherParams& p = lp.p;
+        const int mode = common_params(p, itemsize, positions_esize, request_ids, request_ids_esize, lengths,
+                                       lengths_esize, table_esize, slot_offsets, offsets_esize, batch, selected,
+                                       width, table_width, request_stride, sink_elements, indirect);
+        require(!p.indices_ready, "gather_layers takes no flag bits");
+        if (mode) require(request_tables, "indirect and mapped gathers need one request table per layer");
+        for (int l = 0; l < n_layers; ++l) {
+            require(positions[l], "null positions address");
+            lp.positions[l] = reinterpret_cast<const void*>(positions[l]);
+            if (mode) {
+                require(request_tables[l], "null request table address");
+                lp.tables[l] = reinterpret_cast<const void*>(request_tables[l]);
+            }
+        }
+        lp.n_layers = n_layers;
+        lp.planes_per_layer = planes_per_layer;
+        set_planes(p, src_planes, dst_planes, n_layers * planes_per_layer);
+        bind_device(device);
+        // Grouped copy for 16-512 B rows of at most two (or four) planes per layer
+        // over 16-byte aligned planes, as the single-layer selection does.
+        LayerGatherKernel kernel = gather_layers_kernel<0, 1>;
+        int slot = 5;
+        if (planes_per_layer <= 4 && p.plane_or % 16 == 0 && p.vec_shift >= 0 && p.vec_shift <= 5) {
+            if (planes_per_layer <= 2) {
+                kernel = gather_layers_kernel<EKV_GATHER_LAYERS_RG, 2>;
+                slot = 6;
+            } else {
+                kernel = gather_layers_kernel<2, 4>;
+                slot = 7;
+            }
+        }
+        const int grid = gather_grid(reinterpret_cast<const void*>(kernel), slot, 0, device, batch * selected);
+        launch_dependent(kernel, dim3(grid), dim3(kGatherThreads), 0, static_cast<cudaStream_t>(stream),
+                         "gather_layers launch", lp);
+        check_launch("gather_layers launch");
     });
 }
 
@@ -597,4 +748,21 @@ extern "C" int ekv_gather_rows_planes(
                             request_ids, request_ids_esize, lengths, lengths_esize, request_table,
                             table_esize, slot_offsets, offsets_esize, batch, selected, width,
                             table_width, request_stride, sink_elements, indirect, device, stream);
+}
+
+extern "C" int ekv_gather_layers(
+    const uint64_t* src_planes, const uint64_t* dst_planes, int n_layers, int planes_per_layer,
+    int64_t itemsize,
+    const uint64_t* positions, int positions_esize,
+    const void* request_ids, int request_ids_esize,
+    const void* lengths, int lengths_esize,
+    const uint64_t* request_tables, int table_esize,
+    const void* slot_offsets, int offsets_esize,
+    int64_t batch, int64_t selected, int64_t width,
+    int64_t table_width, int64_t request_stride, int64_t sink_elements,
+    int indirect, int device, void* stream) {
+    return ekv::gather_layers_impl(src_planes, dst_planes, n_layers, planes_per_layer, itemsize, positions,
+                                   positions_esize, request_ids, request_ids_esize, lengths, lengths_esize,
+                                   request_tables, table_esize, slot_offsets, offsets_esize, batch, selected,
+                                   width, table_width, request_stride, sink_elements, indirect, device, stream);
 }

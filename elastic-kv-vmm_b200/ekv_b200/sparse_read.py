@@ -9,7 +9,7 @@ use.
 
 from __future__ import annotations
 
-from ._lib import MAX_PLANES, call, index_esize, last_error, require_cuda, stream_handle, torch_binding, u64_array
+from ._lib import MAX_LAYERS, MAX_PLANES, call, index_esize, last_error, require_cuda, stream_handle, torch_binding, u64_array
 
 INDICES_READY = 16  # EKV_GATHER_INDICES_READY of include/ekv_kernels.h
 
@@ -216,3 +216,84 @@ class PlaneGather:
 
 
 __all__ = ["gather_rows", "gather_rows_planes", "PlaneGather"]
+
+
+class LayerGather:
+    """Every layer's own Top-K gather in one launch (``ekv_gather_layers``).
+
+    ``planes`` / ``outputs`` list every layer's planes layer-major
+    (``planes_per_layer`` each, e.g. K and V); ``positions[l]`` and, in indirect
+    or mapped mode, ``request_tables[l]`` are layer l's.  Layer l's result is
+    that of ``gather_rows_planes`` over its planes with its positions and
+    table; request ids, lengths, slot offsets and ``layout`` are shared.  For a
+    decode step whose every layer's Top-K is known when the step starts; a
+    step that learns layer l's Top-K only after layer l-1 calls the per-layer
+    ``PlaneGather`` instead.  Pointer tables are bound at construction, so the
+    tensors passed here must outlive the object and keep their storage.
+    """
+
+    def __init__(self, planes, positions, request_ids, lengths, request_tables, slot_offsets,
+                 outputs, layout, *, planes_per_layer, indirect, mapped=False):
+        planes, outputs, positions = list(planes), list(outputs), list(positions)
+        n_layers = len(positions)
+        if not 1 <= n_layers <= MAX_LAYERS:
+            raise ValueError("need 1..EKV_MAX_LAYERS layers")
+        if planes_per_layer < 1 or len(planes) != n_layers * planes_per_layer or len(outputs) != len(planes):
+            raise ValueError("need planes_per_layer planes and outputs per layer")
+        if len(planes) > MAX_PLANES:
+            raise ValueError("more than EKV_MAX_PLANES planes")
+        mode = _mode(indirect, mapped)
+        tables = list(request_tables) if mode else [None] * n_layers
+        if len(tables) != n_layers or (mode and any(t is None for t in tables)):
+            raise ValueError("indirect and mapped gathers need one request table per layer")
+        if mode == 1 and slot_offsets is None:
+            raise ValueError("indirect gather needs request_table and slot_offsets")
+        batch, selected = positions[0].shape
+        for pos, table in zip(positions, tables):
+            if pos.shape != (batch, selected) or pos.dtype != positions[0].dtype:
+                raise ValueError("every layer's positions must share one shape and dtype")
+            if table is not None and (table.shape != tables[0].shape or table.dtype != tables[0].dtype):
+                raise ValueError("every layer's request table must share one shape and dtype")
+        for output in outputs:
+            if output.shape != (batch, selected, layout.row_elements):
+                raise ValueError("output shape does not match positions and row width")
+        index = dict(request_ids=request_ids, lengths=lengths, slot_offsets=slot_offsets if mode == 1 else None)
+        index.update({f"positions[{i}]": t for i, t in enumerate(positions)})
+        index.update({f"request_tables[{i}]": t for i, t in enumerate(tables) if t is not None})
+        self.device = require_cuda(index)
+        _check_contiguous(index)
+        for plane, output in zip(planes, outputs):
+            require_cuda(dict(plane=plane, output=output), self.device)
+            if not plane.is_contiguous() or not output.is_contiguous():
+                raise ValueError("planes and outputs must be contiguous")
+            if plane.dtype != output.dtype or plane.dtype != planes[0].dtype:
+                raise TypeError("all planes and outputs must share one dtype")
+        self._keep = (planes, outputs, positions, tables, index)
+        self._src = u64_array(t.data_ptr() for t in planes)
+        self._dst = u64_array(t.data_ptr() for t in outputs)
+        self._positions = u64_array(t.data_ptr() for t in positions)
+        self._tables = u64_array(t.data_ptr() for t in tables) if mode else None
+        table_width = tables[0].shape[-1] if mode == 2 else layout.max_tokens
+        offsets = slot_offsets if mode == 1 else None
+        self._args = (
+            self._src, self._dst, n_layers, planes_per_layer, planes[0].element_size(),
+            self._positions, index_esize(positions[0], "positions"),
+            request_ids.data_ptr(), index_esize(request_ids, "request_ids"),
+            lengths.data_ptr(), index_esize(lengths, "lengths"),
+            self._tables, index_esize(tables[0], "request_table") if mode else 8,
+            None if offsets is None else offsets.data_ptr(),
+            8 if offsets is None else index_esize(offsets, "slot_offsets"),
+            batch, selected, layout.row_elements,
+            table_width, layout.request_bytes // layout.itemsize,
+            layout.chunk_bytes // layout.itemsize,
+            mode, self.device.index,
+        )
+        self.empty = not batch or not selected
+
+    def __call__(self, stream: int | None = None) -> None:
+        if self.empty:
+            return
+        if stream is None:
+            stream = stream_handle(self.device)
+        call("ekv_gather_layers", *self._args, stream)
+

@@ -140,6 +140,32 @@ int ekv_gather_rows_planes(
     int indirect, int device, void* stream);
 
 /*
+ * R3, batched over layers — every layer's own row selection in one launch: layer
+ * l (l < n_layers <= EKV_MAX_LAYERS) is ekv_gather_rows_planes over planes
+ * l*planes_per_layer .. (l+1)*planes_per_layer - 1 of src_planes / dst_planes
+ * with positions[l] and request_tables[l] (HOST arrays of n_layers device
+ * addresses; request_tables may be NULL in direct mode).  request_ids, lengths,
+ * slot_offsets and the geometry are shared by all layers;
+ * n_layers * planes_per_layer <= EKV_MAX_PLANES.  No flag bits.  For a decode
+ * step whose every layer's Top-K is known when the step starts: the same bytes
+ * as n_layers per-layer calls, without a launch boundary between layers.  The
+ * per-layer entry points above replace the reference's per-layer calls; this one
+ * has no reference counterpart.
+ */
+#define EKV_MAX_LAYERS 128
+int ekv_gather_layers(
+    const uint64_t* src_planes, const uint64_t* dst_planes, int n_layers, int planes_per_layer,
+    int64_t itemsize,
+    const uint64_t* positions, int positions_esize,
+    const void* request_ids, int request_ids_esize,
+    const void* lengths, int lengths_esize,
+    const uint64_t* request_tables, int table_esize,
+    const void* slot_offsets, int offsets_esize,
+    int64_t batch, int64_t selected, int64_t width,
+    int64_t table_width, int64_t request_stride, int64_t sink_elements,
+    int indirect, int device, void* stream);
+
+/*
  * R5 — migration row copies between KV planes and a staging buffer.  Replaces
  * the data movement of HostKVCache.backup_from_device_all_layer /
  * load_to_device_per_layer called at adaptive_sparse/migration.py:109-111 and

@@ -487,3 +487,84 @@ def test_grouped_small_rows_match_the_oracle(row_bytes, n_planes, mode, cuda_dev
     for out, other, exp in zip(outs, again, want):
         np.testing.assert_array_equal(out.cpu().numpy(), exp)
         np.testing.assert_array_equal(other.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("row_bytes", [6, 16, 48, 256, 512, 1024, 2048])
+@pytest.mark.parametrize("planes_per_layer", [1, 2, 3])
+@pytest.mark.parametrize("mode", ["direct", "indirect", "mapped"])
+@pytest.mark.parametrize("layers", [1, 5])
+def test_layer_gather_matches_the_oracle_per_layer(row_bytes, planes_per_layer, mode, layers, cuda_device):
+    """One ekv_gather_layers launch writes, for every layer, what the oracle's
+    gather of that layer's planes with that layer's positions and table gives:
+    every copy instance (grouped, flattened, per-row off the 16-byte grid), every
+    addressing mode, zero rows for positions outside [0, length)."""
+    from ekv_b200.sparse_read import LayerGather
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    width = row_bytes // 2
+    gen = torch.Generator().manual_seed(row_bytes * 1000 + planes_per_layer * 10 + layers)
+    batch, tokens, selected = 5, 64, 97
+    layout = VirtualKVLayout(batch, tokens, width, itemsize=2, chunk_bytes=4096)
+    elems = layout.capacity_bytes // 2
+    ids = torch.randperm(batch, generator=gen)
+    lengths = torch.randint(0, tokens + 1, (batch,), generator=gen)
+    lengths[1] = tokens
+    n_logical = batch * tokens
+    first = layout.chunk_bytes // 2
+    offsets = first + torch.randperm((elems - first) // width, generator=gen)[:n_logical] * width
+    rows_per_request = layout.request_bytes // row_bytes
+    planes, outs, positions, tables = [], [], [], []
+    for layer in range(layers):
+        planes += [torch.randint(-30000, 30000, (elems,), generator=gen, dtype=torch.int16)
+                   for _ in range(planes_per_layer)]
+        outs += [torch.full((batch, selected, width), 9, dtype=torch.int16, device=cuda_device)
+                 for _ in range(planes_per_layer)]
+        pos = torch.randint(-3, tokens + 3, (batch, selected), generator=gen)
+        if mode == "indirect":
+            table = torch.randperm(n_logical, generator=gen).view(batch, tokens)
+            if layer == layers - 1:
+                # an odd element offset: this batch leaves the 16-byte grid
+                offsets[table[int(ids[1]), 5]] = first + 1
+                pos[1, 2] = 5
+        else:
+            table = torch.randint(-1, rows_per_request + 2, (batch, tokens), generator=gen)
+        positions.append(pos)
+        tables.append(table)
+    dev = lambda t: t.to(cuda_device)  # noqa: E731
+    indirect, mapped = mode == "indirect", mode == "mapped"
+    gather = LayerGather([dev(p).view(torch.bfloat16) for p in planes], [dev(p) for p in positions], dev(ids),
+                         dev(lengths), [dev(t) for t in tables] if mode != "direct" else None,
+                         dev(offsets) if indirect else None, [o.view(torch.bfloat16) for o in outs], layout,
+                         planes_per_layer=planes_per_layer, indirect=indirect, mapped=mapped)
+    gather()
+    torch.cuda.synchronize()
+    for layer in range(layers):
+        sl = slice(layer * planes_per_layer, (layer + 1) * planes_per_layer)
+        want = og.gather_rows_planes([p.numpy() for p in planes[sl]], positions[layer].numpy(), ids.numpy(),
+                                     lengths.numpy(), tables[layer].numpy() if mode != "direct" else None,
+                                     offsets.numpy() if indirect else None, width=width, table_width=tokens,
+                                     request_stride=layout.request_bytes // 2,
+                                     sink_elements=layout.chunk_bytes // 2, indirect=indirect, mapped=mapped)
+        for out, exp in zip(outs[sl], want):
+            np.testing.assert_array_equal(out.cpu().numpy(), exp)
+
+
+def test_layer_gather_checks_its_arguments(cuda_device):
+    from ekv_b200.sparse_read import LayerGather
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    layout = VirtualKVLayout(2, 16, 128, itemsize=2, chunk_bytes=4096)
+    plane = torch.zeros(layout.capacity_bytes // 2, dtype=torch.bfloat16, device=cuda_device)
+    out = torch.zeros((2, 4, 128), dtype=torch.bfloat16, device=cuda_device)
+    pos = torch.zeros((2, 4), dtype=torch.int32, device=cuda_device)
+    ids = torch.arange(2, device=cuda_device)
+    lengths = torch.full((2,), 16, device=cuda_device)
+    with pytest.raises(ValueError, match="planes_per_layer"):
+        LayerGather([plane] * 3, [pos, pos], ids, lengths, None, None, [out] * 3, layout, planes_per_layer=2,
+                    indirect=False)
+    with pytest.raises(ValueError, match="one request table per layer"):
+        LayerGather([plane] * 4, [pos, pos], ids, lengths, [pos], None, [out] * 4, layout, planes_per_layer=2,
+                    indirect=False, mapped=True)
+    with pytest.raises(ValueError, match="EKV_MAX_LAYERS"):
+        LayerGather([plane] * 129, [pos] * 129, ids, lengths, None, None, [out] * 129, layout,
+                    planes_per_layer=1, indirect=False)

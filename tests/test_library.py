@@ -54,6 +54,15 @@ def test_entry_points_validate_before_touching_a_device(library_path):
     rc = lib.ekv_gather_rows_planes(None, None, 0, 2, None, 4, None, 4, None, 4, None, 8, None, 8,
                                     1, 1, 1, 1, 1, 0, 1, 0, None)
     assert rc == -1 and b"plane count" in lib.ekv_error()
+    rc = lib.ekv_gather_layers(None, None, 0, 2, 2, None, 4, None, 4, None, 4, None, 8, None, 8,
+                               1, 1, 1, 1, 1, 0, 2, 0, None)
+    assert rc == -1 and b"layer count" in lib.ekv_error()
+    rc = lib.ekv_gather_layers(None, None, 129, 2, 2, None, 4, None, 4, None, 4, None, 8, None, 8,
+                               1, 1, 1, 1, 1, 0, 2, 0, None)
+    assert rc == -1 and b"layer count" in lib.ekv_error()
+    rc = lib.ekv_gather_layers(None, None, 100, 3, 2, None, 4, None, 4, None, 4, None, 8, None, 8,
+                               1, 1, 1, 1, 1, 0, 2, 0, None)
+    assert rc == -1 and b"planes_per_layer" in lib.ekv_error()
     rc = lib.ekv_resolve_resident(None, 4, 0, 0, 1, None, 4, 0, 0, None, 8, 0, None, 8, 0, None, 4, 0,
                                   None, 8, 0, 1, None, 0, 0, 0, 0, None)
     assert rc == -1 and b"block_size" in lib.ekv_error()
