@@ -20,7 +20,9 @@
 // the widest element size that divides every address.  (A bulk-copy, TMA
 // engine, variant measured 0.89 of the copy peak at 2 KiB rows and was bound by
 // the bulk-operation rate at smaller rows, so the register-staged kernel is the
-// only one.)
+// only one.)  When each layer has its own row selection, ekv_gather_layers runs
+// every layer's gather in one launch (gather_layers_kernel), so short per-layer
+// launches do not each pay a ramp, a tail and a dependency wait.
 #include <atomic>
 
 #include "common.cuh"
