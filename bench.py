@@ -32,9 +32,11 @@ decode step, then the freeable-bitmap build and its cross-rank AND-combine, all
 inside the timed step (``--skip-config4`` leaves it out).
 
 ``--config 4`` / ``--config 5`` time the decode-step configurations instead (one
-JSON line each): config 4 reports its concurrent form (each layer's lookup beside
-its mapped gather) with the plain layer order and the Top-K-ahead pipelined order
-in ``step_forms``; config 5 reports the swap-in pipeline with the plain layer
+JSON line each): config 4 reports its fused form (each layer's lookup and mapped
+gather in one launch, the miss-list compaction beside the next layer) with the
+concurrent form (the lookup beside the mapped gather), the plain layer order, and
+the two forms that need every layer's Top-K up front (pipelined, multi-layer) in
+``step_forms``; config 5 reports the swap-in pipeline with the plain layer
 order as ``sequential_ms_per_step``.
 
 ``--impl reference`` times the reference's CPU path (torch-CPU restatement,
@@ -1173,6 +1175,19 @@ def run_default(args, dist: Dist):
 
 CFG4 = dict(layers=48, kv_heads=8, head_dim=128, requests=32, context=131072, hot=4096, topk=2048,
             hit_fraction=0.9)
+# The two config-4 step forms that hold when layer i's Top-K is known only after layer
+# i-1; the reported one is timed with the combine variants too.
+CFG4_FORMS = {
+    "fused": "each layer's lookup and mapped K,V gather in ONE launch (ekv_lookup_gather_planes: the slot "
+             "read once from the residency map, slots and miss mask written beside the rows), back to back "
+             "on the step's stream, and layer i's miss-list compaction from the mask (ekv_compact_misses) on "
+             "a second stream beside layer i+1 (LayerPipeline)",
+    "concurrent": "the mapped K,V gathers (slot read from the residency map) back to back on the step's "
+                  "stream, each layer's lookup (slots, miss mask, miss list) forked onto a second stream at "
+                  "the start of its layer and joined at the end of the step (LayerPipeline wait=False); the "
+                  "map is read twice per layer",
+}
+CFG4_REPORTED = "fused"
 
 
 def config4_leg(args, dist: Dist, steps: int, warmup: int):
@@ -1186,10 +1201,11 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     runtime_value.py:167-214).  The layers' launches are replayed from one CUDA
     graph; the bitmap build runs eagerly on a second stream beside them and the
     exchange + AND after them, inside the timed step (build and exchange after the
-    layers, and both beside them, are timed too).  Reported: each layer's lookup
-    beside its mapped gather (the gather reads slots from the residency map, not from
-    the lookup), which holds when layer i's Top-K is known only after layer i-1; timed
-    beside it: the plain layer order (lookup, then the direct gather of its slots), and
+    layers, and both beside them, are timed too).  Reported: CFG4_REPORTED, the fused
+    form (each layer's lookup and mapped gather in one launch, its miss list compacted
+    beside the next layer), which holds when layer i's Top-K is known only after layer
+    i-1; timed beside it: the concurrent form (each layer's lookup beside its mapped
+    gather), the plain layer order (lookup, then the direct gather of its slots), and
     two forms that need every layer's Top-K up front -- the pipelined order (layer i's
     gather beside layer i+1's lookup) and the multi-layer form (one lookup launch over
     all layers, then one ekv_gather_layers launch)."""
@@ -1198,7 +1214,7 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     from ekv_b200.pipeline import LayerPipeline
     from ekv_b200.releasable import bitmap_to_chunks, combine_freeable, freeable_bitmap
     from ekv_b200.resident_lookup import LookupPlan
-    from ekv_b200.sparse_read import LayerGather, PlaneGather
+    from ekv_b200.sparse_read import LayerGather, LookupGather, PlaneGather
     from ekv_b200.virtual_layout import VirtualKVLayout
     from oracle import gather as og
     from oracle import lookup as ol
@@ -1256,6 +1272,12 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
               for layer in range(layers)]
     pipelines = {"concurrent": LayerPipeline(lookups, mapped, dev, wait=False),
                  "pipelined": LayerPipeline(lookups, gathers, dev)}
+    # Fused: each layer's lookup and mapped gather in ONE launch (the map read once),
+    # back to back on the step's stream, and the miss-list compaction of layer i from
+    # the miss mask on a second stream beside layer i+1; valid for per-layer Top-K.
+    fused = [LookupGather(planes[2 * layer:2 * layer + 2], maps[layer], topks[layer], req_ids, ctx_lengths,
+                          outs[2 * layer:2 * layer + 2], layout, indices_ready=True) for layer in range(layers)]
+    pipelines["fused"] = LayerPipeline(fused, [f.compact for f in fused], dev)
     # Every layer's Top-K known when the step starts: one lookup launch over all layers'
     # rows (the stacked maps and Top-K as layers x requests rows), then every layer's
     # direct K,V gather of its slots in one ekv_gather_layers launch.  Each residency-map
@@ -1272,7 +1294,7 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
 
     pipelines["multi_layer"] = multi_layer_step
     pipelines["multi_layer_gather"] = layer_gather  # the gather launch alone: its kernel's roofline
-    modes = ("order", "concurrent", "pipelined", "multi_layer")
+    modes = ("order", "fused", "concurrent", "pipelined", "multi_layer")
     projection, refs, mapped_bits, candidate, unmapped, n_chunks, _ = freeable_world(dist, shard)
     counts_buf = projection.counts(candidate)
     bits_buf = freeable_bitmap(counts_buf, refs, mapped_bits)
@@ -1310,6 +1332,7 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
                    all_lookup.miss_count.view(layers, reqs)[-1])
     for mode in modes[1:]:
         last_lookup = last_of_all if mode == "multi_layer" else \
+            (fused[-1].slots, fused[-1].miss_list, fused[-1].miss_count) if mode == "fused" else \
             (lookups[-1].slots, lookups[-1].miss_list, lookups[-1].miss_count)
         for t in (*outs, *last_lookup):
             t.zero_()
@@ -1374,12 +1397,13 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
             joint["bits"] = combine_freeable(bits_buf)
 
     mode_ms = {}
+    reported = CFG4_REPORTED
     with ClockSampler(dist.local_rank) as clocks:
         for mode in modes:
             mode_ms[mode] = timed(lambda: step(mode), steps, warmup, dist) / steps
-        after_ms = timed(lambda: step("concurrent", combine="after"), steps, warmup, dist) / steps
-        second_stream_ms = timed(lambda: step("concurrent", combine="second_stream"), steps, warmup, dist) / steps
-        without_combine_ms = timed(lambda: replay("concurrent"), steps, warmup, dist) / steps
+        after_ms = timed(lambda: step(reported, combine="after"), steps, warmup, dist) / steps
+        second_stream_ms = timed(lambda: step(reported, combine="second_stream"), steps, warmup, dist) / steps
+        without_combine_ms = timed(lambda: replay(reported), steps, warmup, dist) / steps
         combine_alone_ms = timed(bitmap_and_combine, steps, warmup, dist) / steps
         layer_gather_ms = timed(lambda: replay("multi_layer_gather"), steps, warmup, dist) / steps
     torch.cuda.synchronize()
@@ -1387,7 +1411,7 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     for r in range(dist.world):
         expected_joint -= unmapped[r]
     joint_ok = bitmap_to_chunks(joint["bits"]) == expected_joint
-    ms_per_step = mode_ms["concurrent"]
+    ms_per_step = mode_ms[reported]
     units = reqs * k * layers
     hits = reqs * n_hits * layers
     misses = units - hits
@@ -1410,11 +1434,10 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
                    "l2": "no flush: each layer gathers into its own output buffers; a step touches "
                          f"{bytes_per_step / 1e9:.2f} GB per GPU (> 126 MB L2)"},
         "step_forms": {
-            "reported": "concurrent: the mapped K,V gathers (slot read from the residency map) back to back "
-                        "on the step's stream, each layer's lookup (slots, miss mask, miss list) forked onto a "
-                        "second stream at the start of its layer and joined at the end of the step "
-                        "(LayerPipeline wait=False), so it holds when layer i's Top-K is known only after "
-                        "layer i-1",
+            "reported": f"{reported}: {CFG4_FORMS[reported]}",
+            **{mode: {"ms_per_step": mode_ms[mode], "value": units / (mode_ms[mode] / 1e3),
+                      "frac": bytes_per_step / (mode_ms[mode] / 1e3) / 1e9 / peak, "what": CFG4_FORMS[mode]}
+               for mode in ("fused", "concurrent") if mode != reported},
             "layer_order": {"ms_per_step": mode_ms["order"], "value": units / (mode_ms["order"] / 1e3),
                             "what": "lookup, then the direct gather of its slots, layer after layer (the "
                                     "reference's order)"},

@@ -60,6 +60,19 @@ _KERNELS = {
         _i64, _i64, _i64, _i64, _i64, _i64,
         _i32, _i32, _p,
     ],
+    "ekv_lookup_gather_planes": [
+        _u64p, _u64p, _i32, _i64,
+        _p, _i32, _p, _i32, _p, _i32, _p, _i32, _i64,
+        _i64, _i64, _i64, _i64, _i64,
+        _p, _p,
+        _i32, _i32, _p,
+    ],
+    "ekv_compact_misses": [
+        _p, _i64, _p, _i32, _i64,
+        _i64, _i64,
+        _p, _i64, _p,
+        _i32, _p,
+    ],
     "ekv_gather_layers": [
         _u64p, _u64p, _i32, _i32, _i64,
         _u64p, _i32, _p, _i32, _p, _i32, _u64p, _i32, _p, _i32,

@@ -44,6 +44,10 @@ struct GatherParams {
     int indices_ready;  // EKV_GATHER_INDICES_READY was set: see first_batch()
     int n_planes;
     int vec_shift;  // log2(row_bytes / 16) when that is a power of two, else -1
+    // Fused lookup (ekv_lookup_gather_planes, mapped mode): row r's slot and miss
+    // flag, [batch, selected] contiguous; null otherwise.
+    int32_t* slots_out;
+    uint8_t* miss_out;
     const char* src[EKV_MAX_PLANES];
     char* dst[EKV_MAX_PLANES];
 };
@@ -97,15 +101,24 @@ constexpr int kUnroll = EKV_GATHER_UNROLL;
 constexpr int64_t kSmallRowBytes = EKV_GATHER_SMALL_ROW_BYTES;
 constexpr int kSmallUnroll = EKV_GATHER_SMALL_UNROLL;
 
+// What a residency lookup reports for a row: its slot (-1 for a position outside
+// the valid range) and whether a valid position had no slot (a miss).
+struct RowLookup {
+    int32_t slot = -1;
+    bool miss = false;
+};
+
 // Byte offset of row r inside every source plane, or valid = false.  `positions`
 // and `table` stand in for p.positions and p.request_table (one layer's of a
-// multi-layer launch).
+// multi-layer launch).  In mapped mode `found` receives the lookup's view of the
+// row.
 __device__ __forceinline__ int64_t resolve_row_at(const GatherParams& p, const void* positions,
-                                                  const void* table, int64_t r, bool& valid) {
+                                                  const void* table, int64_t r, bool& valid, RowLookup& found) {
     const int64_t b = r / p.selected;
     const int64_t pos = load_index(positions, p.pos_es, r);
     const int64_t length = load_index(p.lengths, p.len_es, b);
-    valid = pos >= 0 && pos < length;
+    // A residency map row has table_width entries: later positions have no slot.
+    valid = pos >= 0 && pos < length && (p.indirect != 2 || pos < p.table_width);
     if (!valid) return 0;
     const int64_t req = load_index(p.request_ids, p.req_es, b);
     int64_t element;
@@ -116,6 +129,8 @@ __device__ __forceinline__ int64_t resolve_row_at(const GatherParams& p, const v
         // Mapped: the table holds the row's slot in the request's fixed region, -1 if
         // absent; a slot past the region reads as absent too (never outside the region).
         const int64_t slot = load_index(table, p.table_es, req * p.table_width + pos);
+        found.slot = static_cast<int32_t>(slot);  // int32 truncation, as ekv_lookup_slots stores it
+        found.miss = slot < 0;
         if (slot < 0 || (slot + 1) * p.width > p.request_stride) {
             valid = false;
             return 0;
@@ -273,17 +288,33 @@ __device__ __forceinline__ void copy_batch_vec16(const GatherParams& p, int64_t 
 // warp's 32-row batch, so the three dependent index loads are paid once per 32 rows.
 __device__ __forceinline__ int64_t resolve_batch_at(const GatherParams& p, const void* positions,
                                                     const void* table, int64_t row0, int64_t warps,
-                                                    int64_t n_rows, unsigned lane) {
+                                                    int64_t n_rows, unsigned lane, RowLookup& found) {
     const int64_t r = row0 + static_cast<int64_t>(lane) * warps;
     bool valid = false;
     int64_t src = 0;
-    if (r < n_rows) src = resolve_row_at(p, positions, table, r, valid);
+    found = RowLookup{};
+    if (r < n_rows) src = resolve_row_at(p, positions, table, r, valid, found);
     return valid ? src : -1;
+}
+
+// The fused lookup's outputs for this lane's row of the batch (a no-op unless the
+// launch carries them).  Called only after the dependency wait.
+__device__ __forceinline__ void emit_lookup(const GatherParams& p, int64_t row0, int64_t warps,
+                                            int64_t n_rows, unsigned lane, const RowLookup& found) {
+    if (!p.slots_out) return;
+    const int64_t r = row0 + static_cast<int64_t>(lane) * warps;
+    if (r < n_rows) {
+        p.slots_out[r] = found.slot;
+        p.miss_out[r] = found.miss ? 1 : 0;
+    }
 }
 
 __device__ __forceinline__ int64_t resolve_batch(const GatherParams& p, int64_t row0, int64_t warps,
                                                  int64_t n_rows, unsigned lane) {
-    return resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane);
+    RowLookup found;
+    const int64_t mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
+    emit_lookup(p, row0, warps, n_rows, lane, found);
+    return mine;
 }
 
 // The first batch's index chain.  With `indices_ready` the caller has promised
@@ -294,10 +325,12 @@ __device__ __forceinline__ int64_t resolve_batch(const GatherParams& p, int64_t 
 __device__ __forceinline__ int64_t first_batch(const GatherParams& p, int64_t row0, int64_t warps,
                                                int64_t n_rows, unsigned lane) {
     int64_t mine = -1;
-    if (p.indices_ready) mine = resolve_batch(p, row0, warps, n_rows, lane);
+    RowLookup found;
+    if (p.indices_ready) mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
     grid_dependency_wait();
     allow_dependents();
-    if (!p.indices_ready) mine = resolve_batch(p, row0, warps, n_rows, lane);
+    if (!p.indices_ready) mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
+    emit_lookup(p, row0, warps, n_rows, lane, found);
     return mine;
 }
 
@@ -479,7 +512,8 @@ gather_layers_kernel(const __grid_constant__ LayerGatherParams lp) {
         for (int64_t row0 = first; row0 < n_rows; row0 += 32 * warps) {
             const int64_t left = (n_rows - row0 + warps - 1) / warps;
             const int nb = static_cast<int>(left < 32 ? left : 32);
-            const int64_t mine = resolve_batch_at(p, positions, table, row0, warps, n_rows, lane);
+            RowLookup found;  // no lookup outputs in the multi-layer launch
+            const int64_t mine = resolve_batch_at(p, positions, table, row0, warps, n_rows, lane, found);
             if (vectors && !__ballot_sync(0xffffffffu, mine >= 0 && (mine & 15))) {
                 if constexpr (kRG > 0) {
                     copy_batch_grouped<kRG, kPL>(p, mine, row0, warps, nb, lane, plane0, per_layer);
@@ -630,7 +664,7 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
                 const void* request_table, int table_esize, const void* slot_offsets,
                 int offsets_esize, int64_t batch, int64_t selected, int64_t width,
                 int64_t table_width, int64_t request_stride, int64_t sink_elements, int indirect,
-                int device, void* stream) {
+                int device, void* stream, int32_t* slots_out = nullptr, uint8_t* miss_out = nullptr) {
     return guarded([&] {
         require(batch >= 0 && selected >= 0 && width >= 0, "sizes must be non-negative");
         require(itemsize > 0, "itemsize must be positive");
@@ -644,8 +678,14 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
                                        width, table_width, request_stride, sink_elements, indirect);
         if (mode == 1) require(request_table, "indirect gather needs request_table and slot_offsets");
         if (mode == 2) require(request_table, "mapped gather needs request_table (the residency map)");
+        if (slots_out || miss_out) {
+            require(mode == 2, "lookup outputs come from a mapped gather");
+            require(slots_out && miss_out, "a fused lookup writes both slots and miss");
+        }
         p.positions = positions;
         p.request_table = request_table;
+        p.slots_out = slots_out;
+        p.miss_out = miss_out;
         set_planes(p, src_planes, dst_planes, n_planes);
         bind_device(device);
         const int64_t n_rows = batch * selected;
@@ -750,6 +790,29 @@ extern "C" int ekv_gather_rows_planes(
                             request_ids, request_ids_esize, lengths, lengths_esize, request_table,
                             table_esize, slot_offsets, offsets_esize, batch, selected, width,
                             table_width, request_stride, sink_elements, indirect, device, stream);
+}
+
+extern "C" int ekv_lookup_gather_planes(
+    const uint64_t* src_planes, const uint64_t* dst_planes, int n_planes, int64_t itemsize,
+    const void* topk, int topk_esize,
+    const void* request_ids, int request_ids_esize,
+    const void* lengths, int lengths_esize,
+    const void* res_map, int map_esize, int64_t map_width,
+    int64_t batch, int64_t k, int64_t width,
+    int64_t request_stride, int64_t sink_elements,
+    int32_t* slots, uint8_t* miss,
+    int flags, int device, void* stream) {
+    const int rc = ekv::guarded([&] {
+        ekv::require((flags & ~EKV_GATHER_INDICES_READY) == 0, "unknown lookup_gather flag bits");
+        if (batch > 0 && k > 0) {
+            ekv::require(width > 0, "width must be positive");
+            ekv::require(slots && miss, "null lookup output");
+        }
+    });
+    if (rc) return rc;
+    return ekv::gather_impl(src_planes, dst_planes, n_planes, itemsize, topk, topk_esize, request_ids,
+                            request_ids_esize, lengths, lengths_esize, res_map, map_esize, nullptr, 8, batch, k,
+                            width, map_width, request_stride, sink_elements, 2 | flags, device, stream, slots, miss);
 }
 
 extern "C" int ekv_gather_layers(

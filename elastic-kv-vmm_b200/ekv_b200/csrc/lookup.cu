@@ -111,6 +111,30 @@ struct LookupParams {
 constexpr int kLookupThreads = EKV_LOOKUP_THREADS;
 constexpr int kLookupWarps = kLookupThreads / 32;
 
+// Exclusive prefix of `count` over the block in thread order (warp shuffle scan,
+// then a scan of the warp totals in shared memory); `total` receives the block's
+// sum.  The caller syncs before `warp_totals` is written again.
+__device__ __forceinline__ int block_exclusive_scan(int count, unsigned lane, int warp, int* warp_totals,
+                                                    int& total) {
+    int inclusive = count;
+#pragma unroll
+    for (int offset = 1; offset < 32; offset <<= 1) {
+        const int other = __shfl_up_sync(0xffffffffu, inclusive, offset);
+        if (lane >= static_cast<unsigned>(offset)) inclusive += other;
+    }
+    if (lane == 31) warp_totals[warp] = inclusive;
+    __syncthreads();
+    int before = 0;
+    total = 0;
+#pragma unroll
+    for (int w = 0; w < kLookupWarps; ++w) {
+        const int warp_count = warp_totals[w];
+        before += w < warp ? warp_count : 0;
+        total += warp_count;
+    }
+    return before + inclusive - count;
+}
+
 // One block per request row; a pass covers kLookupThreads * kItems Top-K
 // columns, each thread kItems consecutive ones, so a row of up to 2048 columns
 // is one pass with all its independent map lookups in flight at once (the
@@ -166,24 +190,10 @@ lookup_kernel(const __grid_constant__ LookupParams p) {
                 }
             }
             // Exclusive prefix of `count` over the block, in thread (= column) order.
-            int inclusive = count;
-#pragma unroll
-            for (int offset = 1; offset < 32; offset <<= 1) {
-                const int other = __shfl_up_sync(0xffffffffu, inclusive, offset);
-                if (lane >= static_cast<unsigned>(offset)) inclusive += other;
-            }
-            if (lane == 31) warp_totals[warp] = inclusive;
-            __syncthreads();
-            int before = 0;
             int total = 0;
-#pragma unroll
-            for (int w = 0; w < kLookupWarps; ++w) {
-                const int warp_count = warp_totals[w];
-                before += w < warp ? warp_count : 0;
-                total += warp_count;
-            }
+            const int before = block_exclusive_scan(count, lane, warp, warp_totals, total);
             if (miss_bits && p.miss_list) {
-                int64_t at = base + before + inclusive - count;
+                int64_t at = base + before;
 #pragma unroll
                 for (int j = 0; j < kLookupItems; ++j) {
                     if ((miss_bits >> j) & 1u) p.miss_list[b * p.list_row + at++] = static_cast<int32_t>(token[j]);
@@ -201,10 +211,101 @@ lookup_kernel(const __grid_constant__ LookupParams p) {
     }
 }
 
+// The miss list and count of a lookup whose slots and miss mask are already
+// written (by a fused lookup + gather, ekv_lookup_gather_planes): the same
+// column-order compaction as lookup_kernel, with the miss bits read from the
+// mask instead of recomputed from the residency map.
+struct CompactParams {
+    const uint8_t* miss;
+    const void* topk;
+    int32_t* miss_list;
+    int32_t* miss_count;
+    int64_t batch, k;
+    int64_t miss_row, topk_row, list_row;
+    int topk_es;
+};
+
+template <int kItems>
+__global__ void __launch_bounds__(kLookupThreads, EKV_LOOKUP_MIN_BLOCKS)
+compact_misses_kernel(const __grid_constant__ CompactParams p) {
+    grid_dependency_wait();
+    allow_dependents();
+    constexpr int kTile = kLookupThreads * kItems;
+    __shared__ int warp_totals[kLookupWarps];
+    const unsigned lane = lane_id();
+    const int warp = threadIdx.x >> 5;
+    for (int64_t b = blockIdx.x; b < p.batch; b += gridDim.x) {
+        int64_t base = 0;
+        for (int64_t c0 = 0; c0 < p.k; c0 += kTile) {
+            const int64_t first = c0 + static_cast<int64_t>(threadIdx.x) * kItems;
+            unsigned miss_bits = 0;
+            int count = 0;
+#pragma unroll
+            for (int j = 0; j < kItems; ++j) {
+                if (first + j < p.k && p.miss[b * p.miss_row + first + j]) {
+                    miss_bits |= 1u << j;
+                    ++count;
+                }
+            }
+            int total = 0;
+            const int before = block_exclusive_scan(count, lane, warp, warp_totals, total);
+            int64_t at = base + before;
+#pragma unroll
+            for (int j = 0; j < kItems; ++j) {
+                if ((miss_bits >> j) & 1u) {
+                    p.miss_list[b * p.list_row + at++] =
+                        static_cast<int32_t>(load_index(p.topk, p.topk_es, b * p.topk_row + first + j));
+                }
+            }
+            base += total;
+            __syncthreads();  // warp_totals is rewritten by the next pass
+        }
+        for (int64_t i = base + threadIdx.x; i < p.k; i += kLookupThreads) {
+            p.miss_list[b * p.list_row + i] = -1;
+        }
+        if (p.miss_count && threadIdx.x == 0) p.miss_count[b] = static_cast<int32_t>(base);
+    }
+}
+
 }  // namespace
 }  // namespace ekv
 
 using namespace ekv;
+
+extern "C" int ekv_compact_misses(
+    const uint8_t* miss, int64_t miss_row_stride,
+    const void* topk, int topk_esize, int64_t topk_row_stride,
+    int64_t batch, int64_t k,
+    int32_t* miss_list, int64_t miss_list_row_stride,
+    int32_t* miss_count,
+    int device, void* stream) {
+    return guarded([&] {
+        require(batch >= 0 && k >= 0, "sizes must be non-negative");
+        if (!batch) return;
+        require(k <= 0x7fffffff, "k must fit in int32");
+        if (k) require(miss && topk && miss_list, "null pointer argument");
+        check_esize(topk_esize, "topk");
+        bind_device(device);
+        CompactParams p{};
+        p.miss = miss;
+        p.topk = topk;
+        p.miss_list = miss_list;
+        p.miss_count = miss_count;
+        p.batch = batch;
+        p.k = k;
+        p.miss_row = miss_row_stride;
+        p.topk_row = topk_row_stride;
+        p.list_row = miss_list_row_stride;
+        p.topk_es = topk_esize;
+        const unsigned grid = static_cast<unsigned>(batch < (1 << 20) ? batch : (1 << 20));
+        auto* kernel = k <= kLookupThreads       ? compact_misses_kernel<1>
+                       : k <= 2 * kLookupThreads ? compact_misses_kernel<2>
+                                                 : compact_misses_kernel<4>;
+        launch_dependent(kernel, dim3(grid), dim3(kLookupThreads), 0, static_cast<cudaStream_t>(stream),
+                         "compact_misses launch", p);
+        check_launch("compact_misses launch");
+    });
+}
 
 extern "C" int ekv_resolve_resident(
     const void* topk, int topk_esize, int64_t topk_row_stride, int64_t topk_col_stride,

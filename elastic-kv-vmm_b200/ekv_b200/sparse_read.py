@@ -215,7 +215,88 @@ class PlaneGather:
         call("ekv_gather_rows_planes", *self._args, stream)
 
 
-__all__ = ["gather_rows", "gather_rows_planes", "PlaneGather"]
+class LookupGather:
+    """One layer's residency lookup and its mapped gather in one launch
+    (``ekv_lookup_gather_planes``); the miss list on request (``compact``).
+
+    ``residency_map`` [R, T] maps token t of request r to its slot in the
+    request's fixed region of every plane (-1: not resident); ``topk`` [B, K]
+    holds token ids, ``request_ids`` [B] the map row / region of each row and
+    ``lengths`` [B] bounds the valid tokens (a token is valid when
+    ``0 <= t < min(lengths[b], T)``).  A call writes ``outputs[p][b, i]`` --
+    plane p's row of the token's slot, zeros for an invalid token, a miss or a
+    slot past the region, as ``gather_rows_planes(..., mapped=True)`` -- and
+    ``slots`` (int32 [B, K]) and ``miss`` (bool [B, K]) as
+    ``lookup_slots(residency_map[request_ids], topk, lengths)`` gives them;
+    ``compact(stream)`` then writes that call's ``miss_list`` and
+    ``miss_count`` from the mask.  Each map entry is read once, where a lookup
+    followed by a gather reads it twice.  Pointer tables and outputs are bound
+    at construction (the tensors passed here must outlive the object);
+    ``indices_ready`` as in ``gather_rows_planes``.
+    """
+
+    def __init__(self, planes, residency_map, topk, request_ids, lengths, outputs, layout, *,
+                 indices_ready=False):
+        planes, outputs = list(planes), list(outputs)
+        if not planes or len(planes) != len(outputs) or len(planes) > MAX_PLANES:
+            raise ValueError("need 1..EKV_MAX_PLANES planes with one output each")
+        if residency_map.dim() != 2 or topk.dim() != 2:
+            raise ValueError("expected residency_map [R, T] and topk [B, K]")
+        batch, k = topk.shape
+        if request_ids.shape != (batch,) or lengths.shape != (batch,):
+            raise ValueError("request_ids and lengths need one entry per Top-K row")
+        for output in outputs:
+            if output.shape != (batch, k, layout.row_elements):
+                raise ValueError("output shape does not match topk and row width")
+        index = dict(residency_map=residency_map, topk=topk, request_ids=request_ids, lengths=lengths)
+        self.device = require_cuda(index)
+        _check_contiguous(index)
+        for plane, output in zip(planes, outputs):
+            require_cuda(dict(plane=plane, output=output), self.device)
+            if not plane.is_contiguous() or not output.is_contiguous():
+                raise ValueError("planes and outputs must be contiguous")
+            if plane.dtype != output.dtype or plane.dtype != planes[0].dtype:
+                raise TypeError("all planes and outputs must share one dtype")
+        import torch
+
+        self.slots = torch.empty((batch, k), dtype=torch.int32, device=self.device)
+        self.miss = torch.empty((batch, k), dtype=torch.bool, device=self.device)
+        self.miss_list = torch.empty((batch, k), dtype=torch.int32, device=self.device)
+        self.miss_count = torch.empty((batch,), dtype=torch.int32, device=self.device)
+        self._keep = (planes, outputs, index)
+        self._src = u64_array(t.data_ptr() for t in planes)
+        self._dst = u64_array(t.data_ptr() for t in outputs)
+        self._args = (
+            self._src, self._dst, len(planes), planes[0].element_size(),
+            topk.data_ptr(), index_esize(topk, "topk"),
+            request_ids.data_ptr(), index_esize(request_ids, "request_ids"),
+            lengths.data_ptr(), index_esize(lengths, "lengths"),
+            residency_map.data_ptr(), index_esize(residency_map, "residency_map"), residency_map.shape[1],
+            batch, k, layout.row_elements,
+            layout.request_bytes // layout.itemsize, layout.chunk_bytes // layout.itemsize,
+            self.slots.data_ptr(), self.miss.data_ptr(),
+            INDICES_READY if indices_ready else 0, self.device.index,
+        )
+        self._compact_args = (
+            self.miss.data_ptr(), k, topk.data_ptr(), index_esize(topk, "topk"), k,
+            batch, k, self.miss_list.data_ptr(), k, self.miss_count.data_ptr(), self.device.index,
+        )
+        self.empty = not batch or not k
+        self._rows = batch
+
+    def __call__(self, stream: int | None = None) -> None:
+        if self.empty:
+            return
+        call("ekv_lookup_gather_planes", *self._args, stream_handle(self.device) if stream is None else stream)
+
+    def compact(self, stream: int | None = None) -> None:
+        """``miss_list`` / ``miss_count`` from the last call's miss mask (launch after it)."""
+        if not self._rows:
+            return
+        call("ekv_compact_misses", *self._compact_args, stream_handle(self.device) if stream is None else stream)
+
+
+__all__ = ["gather_rows", "gather_rows_planes", "PlaneGather", "LookupGather", "LayerGather"]
 
 
 class LayerGather:

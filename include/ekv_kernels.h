@@ -98,7 +98,8 @@ int ekv_lookup_slots(
  *     out[(b*selected + i)*width + c] = valid ? raw[off + c] : 0,  c < width
  * Modes 0 and 1 are the reference's direct and software-table addressing; mode
  * 2 ("mapped", new) reads a residency map (token -> slot in the request's fixed
- * region, -1 = absent) so a lookup and its gather are one launch.
+ * region, -1 = absent) so a lookup and its gather are one launch; there a position
+ * must also be below table_width (the map's row width) to be valid.
  * Offsets, strides and width are counted in elements of `itemsize` bytes; the
  * payload is copied bit for bit.  Index arrays are contiguous.
  *
@@ -138,6 +139,48 @@ int ekv_gather_rows_planes(
     int64_t batch, int64_t selected, int64_t width,
     int64_t table_width, int64_t request_stride, int64_t sink_elements,
     int indirect, int device, void* stream);
+
+/*
+ * R2 + R3 fused — one layer's lookup_slots and its mapped gather in one launch,
+ * so each residency-map entry is read once per layer instead of once by the
+ * lookup and again by the gather.  No reference counterpart: the reference
+ * resolves a layer's Top-K (request_residency.py:819-826) and then reads the
+ * rows (sparse_read.py:33-51) in separate launches.  res_map is [batch', map_width]
+ * contiguous; request_ids[b] picks row b's map row and region; for b < batch, i < k:
+ *     t = topk[b*k + i];  n = min(lengths[b], map_width);  valid = 0 <= t < n
+ *     s = valid ? res_map[request_ids[b]*map_width + t] : -1
+ *     slots[b*k + i] = s (int32);  miss[b*k + i] = valid && s < 0
+ * and plane p's output row (b, i) is ekv_gather_rows_planes in mapped mode (2)
+ * with positions = topk, request_table = res_map, table_width = map_width.  With
+ * request_ids = 0..batch-1, slots and miss equal ekv_lookup_slots' on the same
+ * map, Top-K and lengths; ekv_compact_misses then gives its miss list and count.
+ * slots and miss are contiguous [batch, k].  flags: 0 or EKV_GATHER_INDICES_READY.
+ */
+int ekv_lookup_gather_planes(
+    const uint64_t* src_planes, const uint64_t* dst_planes, int n_planes, int64_t itemsize,
+    const void* topk, int topk_esize,
+    const void* request_ids, int request_ids_esize,
+    const void* lengths, int lengths_esize,
+    const void* res_map, int map_esize, int64_t map_width,
+    int64_t batch, int64_t k, int64_t width,
+    int64_t request_stride, int64_t sink_elements,
+    int32_t* slots, uint8_t* miss,
+    int flags, int device, void* stream);
+
+/*
+ * R2's miss-list compaction from a miss mask already written (by
+ * ekv_lookup_gather_planes): miss_list[b, :] holds topk[b, i] for every i with
+ * miss[b, i] != 0 in ascending i order, then -1 up to k; miss_count[b] (may be
+ * NULL) is their number -- ekv_lookup_slots' miss_list and miss_count for the
+ * same mask.  No reference counterpart (a part of R2).
+ */
+int ekv_compact_misses(
+    const uint8_t* miss, int64_t miss_row_stride,
+    const void* topk, int topk_esize, int64_t topk_row_stride,
+    int64_t batch, int64_t k,
+    int32_t* miss_list, int64_t miss_list_row_stride,
+    int32_t* miss_count,
+    int device, void* stream);
 
 /*
  * R3, batched over layers — every layer's own row selection in one launch: layer

@@ -14,13 +14,14 @@ def row_offsets(positions, request_ids, lengths, request_table, slot_offsets, *,
     (:24-26); direct offset = sink + req * request_stride + pos * width (:28).
     ``mapped`` is this build's third mode (no reference counterpart): the table
     holds the row's slot s in the request's fixed region, valid only when
-    0 <= s and (s + 1) * width <= request_stride; offset = sink + req *
-    request_stride + s * width.
+    pos < table_width (the map's row width), 0 <= s and (s + 1) * width <=
+    request_stride; offset = sink + req * request_stride + s * width.
     """
     pos = positions.astype(np.int64)
     req = request_ids.astype(np.int64)[:, None]
     valid = (pos >= 0) & (pos < lengths.astype(np.int64)[:, None])
     if mapped:
+        valid &= pos < table_width
         flat = request_table.reshape(-1).astype(np.int64)
         slot = np.where(valid, flat[np.where(valid, req * table_width + pos, 0)], -1)
         valid &= (slot >= 0) & ((slot + 1) * width <= request_stride)

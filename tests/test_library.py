@@ -23,7 +23,7 @@ def declared_symbols():
 def test_headers_declare_the_full_abi():
     names = declared_symbols()
     assert {"ekv_error", "ekv_resolve_resident", "ekv_lookup_slots", "ekv_gather_rows",
-            "ekv_gather_rows_planes", "ekv_pack_rows", "ekv_unpack_rows", "ekv_chunk_counts",
+            "ekv_gather_rows_planes", "ekv_lookup_gather_planes", "ekv_compact_misses", "ekv_pack_rows", "ekv_unpack_rows", "ekv_chunk_counts",
             "ekv_freeable_bitmap", "ekv_bitmap_and", "ev_create", "ev_ensure", "ev_precommit",
             "ev_drop", "ev_base", "ev_backed", "ev_reserved", "ev_granularity", "ev_poisoned",
             "ev_error", "ev_close"} <= names
@@ -66,8 +66,17 @@ def test_entry_points_validate_before_touching_a_device(library_path):
     rc = lib.ekv_resolve_resident(None, 4, 0, 0, 1, None, 4, 0, 0, None, 8, 0, None, 8, 0, None, 4, 0,
                                   None, 8, 0, 1, None, 0, 0, 0, 0, None)
     assert rc == -1 and b"block_size" in lib.ekv_error()
+    rc = lib.ekv_lookup_gather_planes(None, None, 1, 2, None, 4, None, 4, None, 4, None, 4, 20,
+                                      1, 1, 1, 0, 0, None, None, 1, 0, None)
+    assert rc == -1 and b"flag bits" in lib.ekv_error()
+    rc = lib.ekv_lookup_gather_planes(None, None, 1, 2, None, 4, None, 4, None, 4, None, 4, 20,
+                                      1, 1, 1, 0, 0, None, None, 0, 0, None)
+    assert rc == -1 and b"null lookup output" in lib.ekv_error()
+    rc = lib.ekv_compact_misses(None, 0, None, 4, 0, 1, 1, None, 0, None, 0, None)
+    assert rc == -1 and b"null pointer" in lib.ekv_error()
     # Empty work is a successful no-op.
     assert lib.ekv_bitmap_and(None, 1, 0, None, 0, None) == 0
+    assert lib.ekv_compact_misses(None, 0, None, 4, 0, 0, 1, None, 0, None, 0, None) == 0
     import torch
 
     if not torch.cuda.is_available():
