@@ -1180,7 +1180,9 @@ CFG4 = dict(layers=48, kv_heads=8, head_dim=128, requests=32, context=131072, ho
 CFG4_FORMS = {
     "fused": "each layer's lookup and mapped K,V gather in ONE launch (ekv_lookup_gather_planes: the slot "
              "read once from the residency map, slots and miss mask written beside the rows), back to back "
-             "on the step's stream, and layer i's miss-list compaction from the mask (ekv_compact_misses) on "
+             "on the step's stream, each marked disjoint from the layers before it (EKV_GATHER_DISJOINT: a "
+             "one-block-per-SM grid that copies while the previous layer drains and waits for it only "
+             "before completing), and layer i's miss-list compaction from the mask (ekv_compact_misses) on "
              "a second stream beside layer i+1 (LayerPipeline)",
     "concurrent": "the mapped K,V gathers (slot read from the residency map) back to back on the step's "
                   "stream, each layer's lookup (slots, miss mask, miss list) forked onto a second stream at "
@@ -1275,8 +1277,11 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     # Fused: each layer's lookup and mapped gather in ONE launch (the map read once),
     # back to back on the step's stream, and the miss-list compaction of layer i from
     # the miss mask on a second stream beside layer i+1; valid for per-layer Top-K.
+    # The layers' launches touch disjoint memory, so each is marked disjoint from the
+    # ones before it: it copies while they drain and waits for them only at its end.
     fused = [LookupGather(planes[2 * layer:2 * layer + 2], maps[layer], topks[layer], req_ids, ctx_lengths,
-                          outs[2 * layer:2 * layer + 2], layout, indices_ready=True) for layer in range(layers)]
+                          outs[2 * layer:2 * layer + 2], layout, indices_ready=True, disjoint=True)
+             for layer in range(layers)]
     pipelines["fused"] = LayerPipeline(fused, [f.compact for f in fused], dev)
     # Every layer's Top-K known when the step starts: one lookup launch over all layers'
     # rows (the stacked maps and Top-K as layers x requests rows), then every layer's

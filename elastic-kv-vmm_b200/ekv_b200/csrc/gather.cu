@@ -42,6 +42,7 @@ struct GatherParams {
     int pos_es, req_es, len_es, table_es, off_es;
     int indirect;       // addressing mode: 0 direct, 1 indirect, 2 mapped
     int indices_ready;  // EKV_GATHER_INDICES_READY was set: see first_batch()
+    int disjoint;       // EKV_GATHER_DISJOINT was set: see first_batch() and finish()
     int n_planes;
     int vec_shift;  // log2(row_bytes / 16) when that is a power of two, else -1
     // Fused lookup (ekv_lookup_gather_planes, mapped mode): row r's slot and miss
@@ -326,12 +327,24 @@ __device__ __forceinline__ int64_t first_batch(const GatherParams& p, int64_t ro
                                                int64_t n_rows, unsigned lane) {
     int64_t mine = -1;
     RowLookup found;
-    if (p.indices_ready) mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
-    grid_dependency_wait();
+    const bool early = p.indices_ready || p.disjoint;
+    if (early) mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
+    // Disjoint: the kernels still running touch nothing this one reads or writes, so
+    // it copies at once and waits for them only before exiting (finish()), which
+    // keeps the stream's order of completion.
+    if (!p.disjoint) grid_dependency_wait();
     allow_dependents();
-    if (!p.indices_ready) mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
+    if (!early) mine = resolve_batch_at(p, p.positions, p.request_table, row0, warps, n_rows, lane, found);
     emit_lookup(p, row0, warps, n_rows, lane, found);
     return mine;
+}
+
+// A disjoint launch completes only after the grids before it: one thread of each
+// block waits for them before the block exits.
+__device__ __forceinline__ void finish(const GatherParams& p) {
+    // No memory clobber: this only holds the block's exit, it orders none of its own
+    // accesses (a clobber here made ptxas spill the copy loops).
+    if (p.disjoint) asm volatile("griddepcontrol.wait;");
 }
 
 // Rows are taken 32 at a time per warp (row0 + k * warps, k < 32); the warp then
@@ -382,6 +395,22 @@ __global__ void __maxnreg__(88) gather_kernel(const __grid_constant__ GatherPara
 __global__ void __launch_bounds__(kGatherThreads, kGatherBlocksPerSM)
 gather_small_rows_kernel(const __grid_constant__ GatherParams p) {
     gather_body<kSmallUnroll, true>(p);
+}
+
+// Disjoint launches (EKV_GATHER_DISJOINT) of the default instance and the two-plane
+// grouped instance (a layer's K and V): the wait before exiting costs ptxas
+// registers (at 88 it spills the copy loops), so these take
+// EKV_GATHER_DISJOINT_MAXNREG; two blocks then fill an SM without room for a lookup
+// block, which the disjoint decode step does not run beside them.  Other instances
+// run a disjoint launch as an ordinary one (waiting before they copy), which is
+// always correct.
+#ifndef EKV_GATHER_DISJOINT_MAXNREG
+#define EKV_GATHER_DISJOINT_MAXNREG 96
+#endif
+__global__ void __maxnreg__(EKV_GATHER_DISJOINT_MAXNREG)
+gather_disjoint_kernel(const __grid_constant__ GatherParams p) {
+    gather_body<kUnroll, false>(p);
+    finish(p);
 }
 
 // Rows of G = row_bytes / 16 vectors per plane, G a power of two of at most 32
@@ -444,8 +473,7 @@ __device__ __forceinline__ void copy_batch_grouped(const GatherParams& p, int64_
 // (40 registers) fill an SM's 64 Ki registers exactly, which the decode step's
 // concurrent form (each layer's lookup beside its gather) relies on.
 template <int kRG, int kPL>
-__global__ void __maxnreg__(88)
-gather_grouped_kernel(const __grid_constant__ GatherParams p) {
+__device__ __forceinline__ void grouped_body(const GatherParams& p) {
     const int64_t n_rows = p.batch * p.selected;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
     const unsigned lane = lane_id();
@@ -464,6 +492,19 @@ gather_grouped_kernel(const __grid_constant__ GatherParams p) {
         }
         mine = resolve_batch(p, row0 + 32 * warps, warps, n_rows, lane);
     }
+}
+
+template <int kRG, int kPL>
+__global__ void __maxnreg__(88)
+gather_grouped_kernel(const __grid_constant__ GatherParams p) {
+    grouped_body<kRG, kPL>(p);
+}
+
+template <int kRG, int kPL>
+__global__ void __maxnreg__(EKV_GATHER_DISJOINT_MAXNREG)
+gather_grouped_disjoint_kernel(const __grid_constant__ GatherParams p) {
+    grouped_body<kRG, kPL>(p);
+    finish(p);
 }
 
 // Multi-layer launch (ekv_gather_layers): layer l gathers its rows with its own
@@ -555,18 +596,29 @@ gather_layers_kernel(const __grid_constant__ LayerGatherParams lp) {
 #define EKV_GATHER_HONOR_READY 1
 #endif
 
+#ifndef EKV_GATHER_DISJOINT_RG
+#define EKV_GATHER_DISJOINT_RG 4  // row groups in flight per lane, disjoint two-plane launches
+#endif
+#ifndef EKV_GATHER_DISJOINT_BLOCKS
+#define EKV_GATHER_DISJOINT_BLOCKS 1  // blocks per SM of a disjoint launch's grid
+#endif
+constexpr int kDisjointSlot = 8, kDisjointGroupedSlot = 9;
+
 using GatherKernel = void (*)(GatherParams);
 
 // The kernel instance for `n_planes` planes of `row_bytes` rows; `slot` names
-// it in the per-device grid cache.
-GatherKernel gather_kernel_for(const GatherParams& p, int& slot, size_t& smem) {
+// it in the per-device grid cache.  A disjoint launch that the chosen instance does
+// not serve as such is cleared to an ordinary one.
+GatherKernel gather_kernel_for(GatherParams& p, int& slot, size_t& smem) {
     smem = 0;
     if (p.n_planes <= EKV_GATHER_GROUPED_MAX_PLANES && p.plane_or % 16 == 0 && p.vec_shift >= 0 &&
         p.vec_shift <= 5) {
         if (p.n_planes <= 2) {
-            slot = 2;
-            return gather_grouped_kernel<4, 2>;
+            slot = p.disjoint ? kDisjointGroupedSlot : 2;
+            return p.disjoint ? gather_grouped_disjoint_kernel<EKV_GATHER_DISJOINT_RG, 2>
+                              : gather_grouped_kernel<4, 2>;
         }
+        p.disjoint = 0;
         if (p.n_planes <= 4) {
             slot = 3;
             return gather_grouped_kernel<3, 4>;
@@ -576,12 +628,17 @@ GatherKernel gather_kernel_for(const GatherParams& p, int& slot, size_t& smem) {
     }
     const bool small = kSmallRowBytes > 0 && p.row_bytes <= kSmallRowBytes &&
                        static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) > kFlatRowLimit;
-    slot = small ? 1 : 0;
-    return small ? gather_small_rows_kernel : gather_kernel;
+    if (small) {
+        p.disjoint = 0;
+        slot = 1;
+        return gather_small_rows_kernel;
+    }
+    slot = p.disjoint ? kDisjointSlot : 0;
+    return p.disjoint ? gather_disjoint_kernel : gather_kernel;
 }
 
 int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n_rows) {
-    static std::atomic<int> cached[8][64];  // per instance and device; a race computes twice
+    static std::atomic<int> cached[10][64];  // per instance and device; a race computes twice
     int grid = device < 64 ? cached[slot][device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
         if (smem > 48 * 1024) {
@@ -590,6 +647,13 @@ int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n
                        "configure gather shared memory");
         }
         grid = persistent_grid(kernel, kGatherThreads, smem, device);
+        if (slot == kDisjointSlot || slot == kDisjointGroupedSlot) {
+            // A disjoint launch leaves SM room for the next one's blocks, which then
+            // become resident and start copying while this one runs: no ramp and
+            // drain between back-to-back launches.
+            const int cap = EKV_GATHER_DISJOINT_BLOCKS * sm_count(device);
+            grid = grid < cap ? grid : cap;
+        }
         if (device < 64) cached[slot][device].store(grid, std::memory_order_relaxed);
     }
     const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
@@ -615,7 +679,7 @@ int common_params(GatherParams& p, int64_t itemsize, int positions_esize, const 
     check_esize(request_ids_esize, "request_ids");
     check_esize(lengths_esize, "lengths");
     const int flags = indirect & ~3;
-    require(flags == 0 || flags == EKV_GATHER_INDICES_READY, "unknown gather flag bits");
+    require((flags & ~(EKV_GATHER_INDICES_READY | EKV_GATHER_DISJOINT)) == 0, "unknown gather flag bits");
     const int mode = indirect & 3;
     require(mode <= 2, "addressing mode must be 0 (direct), 1 (indirect) or 2 (mapped)");
     if (mode == 1) {
@@ -640,7 +704,8 @@ int common_params(GatherParams& p, int64_t itemsize, int positions_esize, const 
     p.table_es = mode ? table_esize : 8;
     p.off_es = mode == 1 ? offsets_esize : 8;
     p.indirect = mode;
-    p.indices_ready = EKV_GATHER_HONOR_READY ? flags != 0 : 0;
+    p.indices_ready = EKV_GATHER_HONOR_READY ? (flags & EKV_GATHER_INDICES_READY) != 0 : 0;
+    p.disjoint = (flags & EKV_GATHER_DISJOINT) != 0;
     p.vec_shift = (p.row_bytes % 16) ? -1 : log2_exact(p.row_bytes / 16);
     return mode;
 }
@@ -721,7 +786,7 @@ int gather_layers_impl(const uint64_t* src_planes, const uint64_t* dst_planes, i
         const int mode = common_params(p, itemsize, positions_esize, request_ids, request_ids_esize, lengths,
                                        lengths_esize, table_esize, slot_offsets, offsets_esize, batch, selected,
                                        width, table_width, request_stride, sink_elements, indirect);
-        require(!p.indices_ready, "gather_layers takes no flag bits");
+        require(!p.indices_ready && !p.disjoint, "gather_layers takes no flag bits");
         if (mode) require(request_tables, "indirect and mapped gathers need one request table per layer");
         for (int l = 0; l < n_layers; ++l) {
             require(positions[l], "null positions address");
@@ -803,7 +868,8 @@ extern "C" int ekv_lookup_gather_planes(
     int32_t* slots, uint8_t* miss,
     int flags, int device, void* stream) {
     const int rc = ekv::guarded([&] {
-        ekv::require((flags & ~EKV_GATHER_INDICES_READY) == 0, "unknown lookup_gather flag bits");
+        ekv::require((flags & ~(EKV_GATHER_INDICES_READY | EKV_GATHER_DISJOINT)) == 0,
+                     "unknown lookup_gather flag bits");
         if (batch > 0 && k > 0) {
             ekv::require(width > 0, "width must be positive");
             ekv::require(slots && miss, "null lookup output");

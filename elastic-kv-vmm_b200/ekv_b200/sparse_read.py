@@ -12,6 +12,7 @@ from __future__ import annotations
 from ._lib import MAX_LAYERS, MAX_PLANES, call, index_esize, last_error, require_cuda, stream_handle, torch_binding, u64_array
 
 INDICES_READY = 16  # EKV_GATHER_INDICES_READY of include/ekv_kernels.h
+DISJOINT = 32  # EKV_GATHER_DISJOINT of include/ekv_kernels.h
 
 
 def _mode(indirect, mapped):
@@ -168,11 +169,12 @@ class PlaneGather:
     the index tensors are fixed at construction, so each call only launches.
 
     The tensors passed here must outlive the object and keep their storage.
-    ``indices_ready`` as in ``gather_rows_planes``.
+    ``indices_ready`` as in ``gather_rows_planes``; ``disjoint`` as in
+    ``LookupGather``.
     """
 
     def __init__(self, planes, positions, request_ids, lengths, request_table, slot_offsets,
-                 outputs, layout, *, indirect, mapped=False, indices_ready=False):
+                 outputs, layout, *, indirect, mapped=False, indices_ready=False, disjoint=False):
         planes = list(planes)
         outputs = list(outputs)
         if not planes or len(planes) != len(outputs) or len(planes) > MAX_PLANES:
@@ -203,7 +205,7 @@ class PlaneGather:
             batch, selected, layout.row_elements,
             table_width, layout.request_bytes // layout.itemsize,
             layout.chunk_bytes // layout.itemsize,
-            mode | (INDICES_READY if indices_ready else 0), self.device.index,
+            mode | (INDICES_READY if indices_ready else 0) | (DISJOINT if disjoint else 0), self.device.index,
         )
         self.empty = not batch or not selected
 
@@ -232,11 +234,16 @@ class LookupGather:
     ``miss_count`` from the mask.  Each map entry is read once, where a lookup
     followed by a gather reads it twice.  Pointer tables and outputs are bound
     at construction (the tensors passed here must outlive the object);
-    ``indices_ready`` as in ``gather_rows_planes``.
+    ``indices_ready`` as in ``gather_rows_planes``.  ``disjoint=True`` promises
+    that no kernel still running when this launch starts (the launches before
+    it on the stream back to the last one without the promise) writes what it
+    reads or touches what it writes -- true of a decode step's back-to-back
+    per-layer launches -- so it copies at once and waits for them only before
+    completing (``EKV_GATHER_DISJOINT``); the bytes are the same either way.
     """
 
     def __init__(self, planes, residency_map, topk, request_ids, lengths, outputs, layout, *,
-                 indices_ready=False):
+                 indices_ready=False, disjoint=False):
         planes, outputs = list(planes), list(outputs)
         if not planes or len(planes) != len(outputs) or len(planes) > MAX_PLANES:
             raise ValueError("need 1..EKV_MAX_PLANES planes with one output each")
@@ -275,7 +282,7 @@ class LookupGather:
             batch, k, layout.row_elements,
             layout.request_bytes // layout.itemsize, layout.chunk_bytes // layout.itemsize,
             self.slots.data_ptr(), self.miss.data_ptr(),
-            INDICES_READY if indices_ready else 0, self.device.index,
+            (INDICES_READY if indices_ready else 0) | (DISJOINT if disjoint else 0), self.device.index,
         )
         self._compact_args = (
             self.miss.data_ptr(), k, topk.data_ptr(), index_esize(topk, "topk"), k,

@@ -111,6 +111,16 @@ int ekv_lookup_slots(
  * for it.  Results are identical either way; only a broken promise can differ.
  */
 #define EKV_GATHER_INDICES_READY 16
+/*
+ * `indirect` may also carry EKV_GATHER_DISJOINT: the caller promises that no kernel
+ * that may still run when this gather starts -- the kernels before it in `stream`
+ * back to the last one launched without this flag -- writes anything the gather
+ * reads or reads or writes anything it writes (e.g. the back-to-back per-layer
+ * gathers of a decode step: disjoint planes, index inputs and outputs).  The gather
+ * then copies at once, while those kernels drain, and waits for them only before
+ * it completes, so the stream's order of completion is kept.
+ */
+#define EKV_GATHER_DISJOINT 32
 int ekv_gather_rows(
     const void* raw, void* out, int64_t itemsize,
     const void* positions, int positions_esize,
@@ -154,7 +164,8 @@ int ekv_gather_rows_planes(
  * with positions = topk, request_table = res_map, table_width = map_width.  With
  * request_ids = 0..batch-1, slots and miss equal ekv_lookup_slots' on the same
  * map, Top-K and lengths; ekv_compact_misses then gives its miss list and count.
- * slots and miss are contiguous [batch, k].  flags: 0 or EKV_GATHER_INDICES_READY.
+ * slots and miss are contiguous [batch, k].  flags: EKV_GATHER_INDICES_READY and/or
+ * EKV_GATHER_DISJOINT.
  */
 int ekv_lookup_gather_planes(
     const uint64_t* src_planes, const uint64_t* dst_planes, int n_planes, int64_t itemsize,

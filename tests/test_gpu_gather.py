@@ -435,7 +435,9 @@ def test_grouped_small_rows_match_the_oracle(row_bytes, n_planes, mode, cuda_dev
     batches (rows not a multiple of 32), invalid positions, empty requests and, in the
     indirect case, a batch holding a row that starts off a 16-byte boundary (element
     copy fallback).  The mapped case also sets the indices-ready flag, whose only
-    effect is when the index chain is walked."""
+    effect is when the index chain is walked; the second launch is marked disjoint
+    (two-plane launches take the disjoint instance, the others run it as an ordinary
+    launch)."""
     from ekv_b200.sparse_read import PlaneGather, gather_rows_planes
     from ekv_b200.virtual_layout import VirtualKVLayout
 
@@ -472,7 +474,7 @@ def test_grouped_small_rows_match_the_oracle(row_bytes, n_planes, mode, cuda_dev
                        indirect=indirect, mapped=mapped, indices_ready=ready)
     again = [torch.full_like(o, 5) for o in outs]
     PlaneGather(dev_planes, *args, [o.view(torch.bfloat16) for o in again], layout,
-                indirect=indirect, mapped=mapped, indices_ready=not ready)()
+                indirect=indirect, mapped=mapped, indices_ready=not ready, disjoint=True)()
     torch.cuda.synchronize()
     if mapped:
         want = og.gather_rows_planes([p.numpy() for p in planes], positions.numpy(), ids.numpy(),

@@ -43,20 +43,21 @@ def _case(row_bytes, n_planes, map_dtype, seed):
 @pytest.mark.parametrize("row_bytes", [6, 256, 512, 2048])
 @pytest.mark.parametrize("n_planes", [1, 2, 5])
 @pytest.mark.parametrize("map_dtype", [torch.int32, torch.int64])
-@pytest.mark.parametrize("ready", [False, True])
-def test_lookup_gather_matches_the_oracle(row_bytes, n_planes, map_dtype, ready, cuda_device):
+@pytest.mark.parametrize("flags", ["none", "ready", "disjoint"])
+def test_lookup_gather_matches_the_oracle(row_bytes, n_planes, map_dtype, flags, cuda_device):
     """Slots, miss mask, miss list, count and every plane's rows bit-equal to the oracle's
     lookup_slots over the selected map rows and its mapped gather, for ragged Top-K rows,
     invalid tokens, an empty request, lengths past the map width and misaligned rows
-    (6-byte rows take the element copy)."""
+    (6-byte rows take the element copy); with no flag, the indices-ready flag and the
+    disjoint flag (which every instance either serves or runs as an ordinary launch)."""
     from ekv_b200.sparse_read import LookupGather
 
-    layout, width, planes, res_map, topk, ids, lengths = _case(row_bytes, n_planes, map_dtype,
-                                                               row_bytes * 10 + n_planes + 7 * ready)
+    seed = row_bytes * 10 + n_planes + 7 * ["none", "ready", "disjoint"].index(flags)
+    layout, width, planes, res_map, topk, ids, lengths = _case(row_bytes, n_planes, map_dtype, seed)
     dev = cuda_device
     outs = [torch.full((topk.shape[0], topk.shape[1], width), 9, dtype=torch.int16, device=dev) for _ in planes]
     fused = LookupGather([p.to(dev) for p in planes], res_map.to(dev), topk.to(dev), ids.to(dev), lengths.to(dev),
-                         outs, layout, indices_ready=ready)
+                         outs, layout, indices_ready=flags == "ready", disjoint=flags == "disjoint")
     fused.miss_list.fill_(123)
     fused()
     fused.compact()
@@ -74,12 +75,13 @@ def test_lookup_gather_matches_the_oracle(row_bytes, n_planes, map_dtype, ready,
         np.testing.assert_array_equal(out.cpu().numpy(), exp)
 
 
-def test_lookup_gather_equals_the_separate_launches(cuda_device):
+@pytest.mark.parametrize("disjoint", [False, True])
+def test_lookup_gather_equals_the_separate_launches(disjoint, cuda_device):
     """At a config-4 layer shape (32 requests x 2048 Top-K, 90 % hits, 256 B rows): the fused
     launch leaves the slots, mask, miss list, count and K/V rows that lookup_slots followed
     by the mapped gather leave, eagerly and replayed from a CUDA graph with the compaction
     on a second stream (LayerPipeline: fused launch, then the compaction beside the next
-    layer)."""
+    layer); also with every launch marked disjoint from the ones before it."""
     from ekv_b200.pipeline import LayerPipeline
     from ekv_b200.resident_lookup import lookup_slots
     from ekv_b200.sparse_read import LookupGather, gather_rows_planes
@@ -108,7 +110,8 @@ def test_lookup_gather_equals_the_separate_launches(cuda_device):
         topks.append(topk)
         planes.append(kv)
         outs.append(out)
-        fused.append(LookupGather(kv, res_map, topk, ids, lengths, out, layout, indices_ready=True))
+        fused.append(LookupGather(kv, res_map, topk, ids, lengths, out, layout, indices_ready=True,
+                                  disjoint=disjoint))
     expected = []
     for layer in range(layers):
         found = lookup_slots(maps[layer], topks[layer], lengths)
