@@ -29,7 +29,9 @@ region).
 ``config4``: config 4 (BASELINE.json's 2/4/8-GPU configuration) measured in the
 same run after the config-2 pool is released: 48 layers of lookup + K,V gather per
 decode step, then the freeable-bitmap build and its cross-rank AND-combine, all
-inside the timed step (``--skip-config4`` leaves it out).
+inside the timed step (``--skip-config4`` leaves it out).  ``config5``, on one GPU:
+config 5's 64 decode steps (lookup -> victim selection -> promotion from pinned host
+history -> gather per layer), as ``--config 5`` reports them (``--skip-config5``).
 
 ``--config 4`` / ``--config 5`` time the decode-step configurations instead (one
 JSON line each): config 4 reports its fused form (each layer's lookup and mapped
@@ -88,6 +90,7 @@ def parse_args(argv=None):
     p.add_argument("--skip-migration", action="store_true")
     p.add_argument("--skip-e2e", action="store_true")
     p.add_argument("--skip-config4", action="store_true", help="skip the config-4 decode-step leg")
+    p.add_argument("--skip-config5", action="store_true", help="skip the config-5 decode leg (1 GPU runs)")
     p.add_argument("--skip-legs", action="store_true",
                    help="measurement aid: skip the bitmap, lookup and shadow side legs (profiling captures)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline time budget")
@@ -1162,13 +1165,22 @@ def run_ours(args, dist: Dist):
 def run_default(args, dist: Dist):
     """The driver's default line: config 2 (``run_ours``), then -- with the config-2 pool
     released -- config 4, BASELINE.json's multi-GPU configuration, as the ``config4``
-    object (every rank takes part)."""
+    object (every rank takes part), and on a single GPU config 5's multi-step decode as
+    the ``config5`` object."""
     result = run_ours(args, dist)
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     if not args.skip_config4:
         config4 = config4_leg(args, dist, args.steps, args.warmup)
         result["config4"] = {key: value for key, value in config4.items()
+                             if key not in ("metric", "higher_is_better", "vs_baseline", "dtype", "n_gpus")}
+    if dist.world == 1 and not args.skip_config5:
+        # Config 5's 64 decode steps on this GPU (24 layers without head sharding), after
+        # config 4's buffers are released.
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        config5 = config5_leg(args, dist, CFG5["steps"])
+        result["config5"] = {key: value for key, value in config5.items()
                              if key not in ("metric", "higher_is_better", "vs_baseline", "dtype", "n_gpus")}
     return result
 
@@ -1529,6 +1541,10 @@ def zipf_topk_schedule(steps, batch, context, k, keep, s, seed):
 
 
 def run_config5(args, dist: Dist):
+    return config5_leg(args, dist, args.steps if args.steps != 100 else CFG5["steps"])
+
+
+def config5_leg(args, dist: Dist, steps: int):
     """Config 5: multi-step sparse decode with host-backed history.  Each step, for every
     layer: lookup of the step's Top-K in the layer's hot buffer, clock victim selection for
     the misses, promotion of the missed rows from pinned host history, mapped gather of all
@@ -1546,7 +1562,6 @@ def run_config5(args, dist: Dist):
     batch, ctx, hot, k = c["requests"], c["context"], c["hot"], c["topk"]
     # 1 GPU without head sharding cannot hold 48 layers of hot buffers (4 GiB per layer).
     layers = args.layers or (c["layers"] if shard > 1 else 24)
-    steps = args.steps if args.steps != 100 else c["steps"]
     # Host history shared by every layer (per-layer history would be 1.5 TiB):
     # word w of token t of request b, plane p = ((b*ctx + t) * words + w) XOR key[p].
     words = row_bytes // 4
