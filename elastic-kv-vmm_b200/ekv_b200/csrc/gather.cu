@@ -339,11 +339,10 @@ __device__ __forceinline__ int64_t first_batch(const GatherParams& p, int64_t ro
     return mine;
 }
 
-// A disjoint launch completes only after the grids before it: one thread of each
-// block waits for them before the block exits.
+// A disjoint launch completes only after the grids before it: its threads wait for
+// them before exiting.  The wait holds the exit and orders none of this kernel's own
+// accesses, so it carries no memory clobber.
 __device__ __forceinline__ void finish(const GatherParams& p) {
-    // No memory clobber: this only holds the block's exit, it orders none of its own
-    // accesses (a clobber here made ptxas spill the copy loops).
     if (p.disjoint) asm volatile("griddepcontrol.wait;");
 }
 
