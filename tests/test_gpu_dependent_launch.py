@@ -1,6 +1,7 @@
 """Dependent launch is a scheduling switch only: a decode step of lookups and gathers gives
 the same bytes, equal to the oracle's, with EKV_B200_PDL=0 (ordinary launches) as with
-the default (programmatic dependent launches).  The switch is read once per process, so
+the default (programmatic dependent launches), including the fused lookup + gather whose
+launches are marked disjoint (they copy before the previous layer completes).  The switch is read once per process, so
 each setting runs in its own child process."""
 
 from __future__ import annotations
@@ -25,7 +26,7 @@ STEP = textwrap.dedent('''
 
     from ekv_b200.pipeline import LayerPipeline
     from ekv_b200.resident_lookup import LookupPlan
-    from ekv_b200.sparse_read import PlaneGather
+    from ekv_b200.sparse_read import LookupGather, PlaneGather
     from ekv_b200.virtual_layout import VirtualKVLayout
     from oracle import gather as og
     from oracle import lookup as ol
@@ -37,7 +38,7 @@ STEP = textwrap.dedent('''
     req_ids = torch.arange(batch, device=dev)
     hot_lengths = torch.full((batch,), hot, dtype=torch.int64, device=dev)
     ctx_lengths = torch.full((batch,), context, dtype=torch.int64, device=dev)
-    saved, keep, lookups, mapped, direct = {}, [], [], [], []
+    saved, keep, lookups, mapped, direct, fused = {}, [], [], [], [], []
     for layer in range(layers):
         res_map = torch.full((batch, context), -1, dtype=torch.int32)
         topk = torch.empty((batch, k), dtype=torch.int32)
@@ -50,7 +51,7 @@ STEP = textwrap.dedent('''
         dmap, dtopk = res_map.to(dev), topk.to(dev)
         dplanes = [p.to(dev).view(torch.bfloat16) for p in planes]
         outs = {form: [torch.full((batch, k, width), 7, dtype=torch.int16, device=dev) for _ in range(2)]
-                for form in ("mapped", "direct")}
+                for form in ("mapped", "direct", "fused")}
         plan = LookupPlan(dmap, dtopk)
         lookups.append(plan)
         mapped.append(PlaneGather(dplanes, dtopk, req_ids, ctx_lengths, dmap, None,
@@ -58,6 +59,10 @@ STEP = textwrap.dedent('''
                                   mapped=True))
         direct.append(PlaneGather(dplanes, plan.slots, req_ids, hot_lengths, None, None,
                                   [o.view(torch.bfloat16) for o in outs["direct"]], layout, indirect=False))
+        # The fused lookup + gather with every launch disjoint from the ones before it.
+        fused.append(LookupGather(dplanes, dmap, dtopk, req_ids, ctx_lengths,
+                                  [o.view(torch.bfloat16) for o in outs["fused"]], layout, indices_ready=True,
+                                  disjoint=True))
         keep.append((dmap, dtopk, dplanes, outs))
         slots = ol.lookup_slots(res_map.numpy(), topk.numpy())[0]
         want = og.gather_rows_planes([p.numpy() for p in planes], slots, req_ids.cpu().numpy(),
@@ -90,7 +95,26 @@ STEP = textwrap.dedent('''
     torch.cuda.synchronize()
     saved.update({f"direct{i}": np.stack([o.cpu().numpy() for o in keep[i][3]["direct"]]) for i in range(layers)})
     saved.update({f"slots{i}": lookups[i].slots.cpu().numpy() for i in range(layers)})
-    del graph
+    saved.update({f"misses{i}": lookups[i].miss_list.cpu().numpy() for i in range(layers)})
+    # The fused disjoint form from one CUDA graph (compaction beside the next layer).
+    fused_step = LayerPipeline(fused, [f.compact for f in fused], dev)
+    with torch.cuda.stream(side):
+        fused_step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    fused_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(fused_graph):
+        fused_step()
+    for i, f in enumerate(fused):
+        f.slots.fill_(-5)
+        f.miss_list.fill_(-5)
+        for o in keep[i][3]["fused"]:
+            o.fill_(7)
+    fused_graph.replay()
+    torch.cuda.synchronize()
+    saved.update({f"fused{i}": np.stack([o.cpu().numpy() for o in keep[i][3]["fused"]]) for i in range(layers)})
+    saved.update({f"fused_slots{i}": fused[i].slots.cpu().numpy() for i in range(layers)})
+    saved.update({f"fused_misses{i}": fused[i].miss_list.cpu().numpy() for i in range(layers)})
+    del graph, fused_graph
     np.savez(sys.argv[1], **saved)
 ''')
 
@@ -111,3 +135,6 @@ def test_dependent_launch_switch_changes_no_bytes(tmp_path):
     for layer in range(4):
         np.testing.assert_array_equal(on[f"mapped{layer}"], on[f"want{layer}"])
         np.testing.assert_array_equal(on[f"direct{layer}"], on[f"want{layer}"])
+        np.testing.assert_array_equal(on[f"fused{layer}"], on[f"want{layer}"])
+        np.testing.assert_array_equal(on[f"fused_slots{layer}"], on[f"slots{layer}"])
+        np.testing.assert_array_equal(on[f"fused_misses{layer}"], on[f"misses{layer}"])
