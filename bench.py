@@ -1315,6 +1315,18 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     projection, refs, mapped_bits, candidate, unmapped, n_chunks, _ = freeable_world(dist, shard)
     counts_buf = projection.counts(candidate)
     bits_buf = freeable_bitmap(counts_buf, refs, mapped_bits)
+    # Across ranks, the alternative to NCCL: one kernel builds this rank's bitmap and ANDs
+    # the peers' over NVLink (symmetric memory, bounded polls), launched beside the layers.
+    peer, peer_error = None, None
+    if dist.world > 1:
+        from ekv_b200.releasable import PeerFreeableCombiner
+
+        try:
+            peer = PeerFreeableCombiner(n_chunks, dev)
+        except Exception as exc:  # every rank meets the same failure (same setup)
+            peer_error = f"{type(exc).__name__}: {exc}"[:200]
+        peer_counts = torch.empty_like(counts_buf)
+        peer_bits = torch.empty_like(bits_buf)
 
     def layers_step(mode="order"):
         if mode in pipelines:
@@ -1406,6 +1418,8 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
         with torch.cuda.stream(bitmap_stream):
             if combine == "second_stream":
                 bitmap_and_combine()
+            elif combine == "peer":
+                peer.combine(projection.counts(candidate, out=peer_counts), refs, mapped_bits, out=peer_bits)
             else:
                 build_bitmap()
         replay(mode)
@@ -1423,11 +1437,20 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
         without_combine_ms = timed(lambda: replay(reported), steps, warmup, dist) / steps
         combine_alone_ms = timed(bitmap_and_combine, steps, warmup, dist) / steps
         layer_gather_ms = timed(lambda: replay("multi_layer_gather"), steps, warmup, dist) / steps
+        peer_ms = timed(lambda: step(reported, combine="peer"), steps, warmup, dist) / steps if peer else None
     torch.cuda.synchronize()
     expected_joint = bitmap_to_chunks(bits_buf)
     for r in range(dist.world):
         expected_joint -= unmapped[r]
     joint_ok = bitmap_to_chunks(joint["bits"]) == expected_joint
+    peer_record = {}
+    if peer is not None:
+        peer_record = {"step_with_peer_combine_beside_ms": peer_ms,
+                       "peer_combine_matches_intersection": bitmap_to_chunks(peer_bits) == expected_joint and not peer.failed(),
+                       "peer_combine": "counts + ekv_freeable_and_peers (build + exchange + AND in one kernel "
+                                       "over NVLink peer memory) on the second stream beside the layers"}
+    elif peer_error:
+        peer_record = {"peer_combine_unavailable": peer_error}
     ms_per_step = mode_ms[reported]
     units = reqs * k * layers
     hits = reqs * n_hits * layers
@@ -1488,12 +1511,13 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
                     "step_with_build_and_exchange_after_the_layers_ms": after_ms,
                     "step_with_combine_on_second_stream_ms": second_stream_ms,
                     "freeable_joint": len(bitmap_to_chunks(joint["bits"])),
-                    "joint_matches_intersection": bool(joint_ok)},
+                    "joint_matches_intersection": bool(joint_ok), **peer_record},
         "parity_layer0_and_last": bool(parity),
         "gpu_launches": (2 * layers + 2) * steps + steps * (dist.world > 1),
         "clocks": clocks.summary(),
     }
     graphs.clear()
+    del peer
     return result
 
 
