@@ -352,12 +352,12 @@ __device__ __forceinline__ void finish(const GatherParams& p) {
 // kU: vectors in flight per lane in the flattened batch copy; kFlatAll: flatten
 // every 16-byte-aligned batch, whatever its row size (the small-row instance,
 // whose rows x planes x vectors stay far below 2^32).
-template <int kU, bool kFlatAll>
+template <int kU, bool kFlatAll, int kWarps = kGatherWarps>
 __device__ __forceinline__ void gather_body(const GatherParams& p) {
     const int64_t n_rows = p.batch * p.selected;
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarps;
     const unsigned lane = lane_id();
-    int64_t row0 = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5);
+    int64_t row0 = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
     int64_t mine = first_batch(p, row0, warps, n_rows, lane);
     const bool small_rows = p.row_bytes % 16 == 0 && p.plane_or % 16 == 0 &&
                             (kFlatAll || static_cast<uint64_t>(p.n_planes) * (p.row_bytes >> 4) <= kFlatRowLimit);
@@ -399,16 +399,27 @@ gather_small_rows_kernel(const __grid_constant__ GatherParams p) {
 // Disjoint launches (EKV_GATHER_DISJOINT) of the default instance and the two-plane
 // grouped instance (a layer's K and V): the wait before exiting costs ptxas
 // registers (at 88 it spills the copy loops), so these take
-// EKV_GATHER_DISJOINT_MAXNREG; two blocks then fill an SM without room for a lookup
-// block, which the disjoint decode step does not run beside them.  Other instances
-// run a disjoint launch as an ordinary one (waiting before they copy), which is
-// always correct.
+// EKV_GATHER_DISJOINT_MAXNREG and leave no room for a lookup block, which the disjoint
+// decode step does not run beside them.  Other instances run a disjoint launch as an
+// ordinary one (waiting before they copy), which is always correct.
 #ifndef EKV_GATHER_DISJOINT_MAXNREG
 #define EKV_GATHER_DISJOINT_MAXNREG 96
 #endif
+// A disjoint launch runs 128-thread blocks, two per SM (8 warps per SM per layer, as the
+// ordinary launch), while registers let five such blocks share an SM: two and a half
+// layers are resident at once and a layer's blocks are replaced one by one as they
+// finish.  Measured on config 4 (48 layers per step, one B200): 256-thread blocks one per
+// SM 0.618 / 3.99 ms at the TP8 / TP1 shard, 128-thread blocks two per SM 0.590 / 3.90,
+// three per SM 0.619 / 3.86, 64-thread blocks four per SM 0.594 / 3.90, five per SM
+// 0.622 / 3.94, 96-thread blocks three per SM 0.616 / 3.97.
+#ifndef EKV_GATHER_DISJOINT_THREADS
+#define EKV_GATHER_DISJOINT_THREADS 128  // threads per block of a disjoint launch
+#endif
+constexpr int kDisjointThreads = EKV_GATHER_DISJOINT_THREADS;
+constexpr int kDisjointWarps = kDisjointThreads / 32;
 __global__ void __maxnreg__(EKV_GATHER_DISJOINT_MAXNREG)
 gather_disjoint_kernel(const __grid_constant__ GatherParams p) {
-    gather_body<kUnroll, false>(p);
+    gather_body<kUnroll, false, kDisjointWarps>(p);
     finish(p);
 }
 
@@ -471,12 +482,12 @@ __device__ __forceinline__ void copy_batch_grouped(const GatherParams& p, int64_
 // At most 88 registers: two of these blocks and one 512-thread lookup block
 // (40 registers) fill an SM's 64 Ki registers exactly, which the decode step's
 // concurrent form (each layer's lookup beside its gather) relies on.
-template <int kRG, int kPL>
+template <int kRG, int kPL, int kWarps = kGatherWarps>
 __device__ __forceinline__ void grouped_body(const GatherParams& p) {
     const int64_t n_rows = p.batch * p.selected;
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * kGatherWarps;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarps;
     const unsigned lane = lane_id();
-    int64_t row0 = static_cast<int64_t>(blockIdx.x) * kGatherWarps + (threadIdx.x >> 5);
+    int64_t row0 = static_cast<int64_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
     int64_t mine = first_batch(p, row0, warps, n_rows, lane);
     for (; row0 < n_rows; row0 += 32 * warps) {
         const int64_t left = (n_rows - row0 + warps - 1) / warps;
@@ -502,7 +513,7 @@ gather_grouped_kernel(const __grid_constant__ GatherParams p) {
 template <int kRG, int kPL>
 __global__ void __maxnreg__(EKV_GATHER_DISJOINT_MAXNREG)
 gather_grouped_disjoint_kernel(const __grid_constant__ GatherParams p) {
-    grouped_body<kRG, kPL>(p);
+    grouped_body<kRG, kPL, kDisjointWarps>(p);
     finish(p);
 }
 
@@ -599,7 +610,7 @@ gather_layers_kernel(const __grid_constant__ LayerGatherParams lp) {
 #define EKV_GATHER_DISJOINT_RG 4  // row groups in flight per lane, disjoint two-plane launches
 #endif
 #ifndef EKV_GATHER_DISJOINT_BLOCKS
-#define EKV_GATHER_DISJOINT_BLOCKS 1  // blocks per SM of a disjoint launch's grid
+#define EKV_GATHER_DISJOINT_BLOCKS 2  // blocks per SM of a disjoint launch's grid
 #endif
 constexpr int kDisjointSlot = 8, kDisjointGroupedSlot = 9;
 
@@ -636,7 +647,7 @@ GatherKernel gather_kernel_for(GatherParams& p, int& slot, size_t& smem) {
     return p.disjoint ? gather_disjoint_kernel : gather_kernel;
 }
 
-int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n_rows) {
+int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n_rows, int threads) {
     static std::atomic<int> cached[10][64];  // per instance and device; a race computes twice
     int grid = device < 64 ? cached[slot][device].load(std::memory_order_relaxed) : 0;
     if (!grid) {
@@ -645,9 +656,9 @@ int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)),
                        "configure gather shared memory");
         }
-        grid = persistent_grid(kernel, kGatherThreads, smem, device);
+        grid = persistent_grid(kernel, threads, smem, device);
         if (slot == kDisjointSlot || slot == kDisjointGroupedSlot) {
-            // A disjoint launch leaves SM room for the next one's blocks, which then
+            // A disjoint launch leaves SM room for the next ones' blocks, which then
             // become resident and start copying while this one runs: no ramp and
             // drain between back-to-back launches.
             const int cap = EKV_GATHER_DISJOINT_BLOCKS * sm_count(device);
@@ -655,7 +666,8 @@ int gather_grid(const void* kernel, int slot, size_t smem, int device, int64_t n
         }
         if (device < 64) cached[slot][device].store(grid, std::memory_order_relaxed);
     }
-    const int64_t needed = (n_rows + kGatherWarps - 1) / kGatherWarps;
+    const int64_t block_warps = threads / 32;
+    const int64_t needed = (n_rows + block_warps - 1) / block_warps;
     return static_cast<int>(needed < grid ? needed : grid);
 }
 
@@ -757,8 +769,9 @@ int gather_impl(const uint64_t* src_planes, const uint64_t* dst_planes, int n_pl
         int slot = 0;
         size_t smem = 0;
         const GatherKernel kernel = gather_kernel_for(p, slot, smem);
-        const int grid = gather_grid(reinterpret_cast<const void*>(kernel), slot, smem, device, n_rows);
-        launch_dependent(kernel, dim3(grid), dim3(kGatherThreads), smem, s, "gather_rows launch", p);
+        const int threads = p.disjoint ? kDisjointThreads : kGatherThreads;
+        const int grid = gather_grid(reinterpret_cast<const void*>(kernel), slot, smem, device, n_rows, threads);
+        launch_dependent(kernel, dim3(grid), dim3(threads), smem, s, "gather_rows launch", p);
         check_launch("gather_rows launch");
     });
 }
@@ -812,7 +825,8 @@ int gather_layers_impl(const uint64_t* src_planes, const uint64_t* dst_planes, i
                 slot = 7;
             }
         }
-        const int grid = gather_grid(reinterpret_cast<const void*>(kernel), slot, 0, device, batch * selected);
+        const int grid = gather_grid(reinterpret_cast<const void*>(kernel), slot, 0, device, batch * selected,
+                                     kGatherThreads);
         launch_dependent(kernel, dim3(grid), dim3(kGatherThreads), 0, static_cast<cudaStream_t>(stream),
                          "gather_layers launch", lp);
         check_launch("gather_layers launch");
