@@ -1431,12 +1431,14 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
         joint["bits"] = combine_freeable(bits_buf)
 
     def step(mode, combine="beside"):
-        # The freeable bitmap depends only on chunk ownership.  "beside" (reported): its
-        # build runs on a second stream beside the layers and the cross-rank exchange + AND
-        # after them.  "after": build and exchange after the layers.  "second_stream": build
-        # and exchange beside the layers -- measured slower across ranks: the gathers'
-        # persistent grids hold every SM, so the NCCL kernels, which wait for the peer
-        # rank's, start late (2 GPUs: +334 us per step against +30 us after the layers).
+        # The freeable bitmap depends only on chunk ownership.  "peer" (reported across
+        # ranks): counts + the fused build/exchange/AND kernel over peer memory on a second
+        # stream beside the layers.  "beside" (reported on one rank): the build on a second
+        # stream beside the layers and the NCCL exchange + AND after them.  "after": build
+        # and NCCL exchange after the layers.  "second_stream": build and NCCL exchange
+        # beside the layers -- measured slower across ranks: the gathers' persistent grids
+        # hold every SM, so the NCCL kernels, which wait for the peer rank's, start late
+        # (2 GPUs: +334 us per step against +30 us after the layers).
         if combine == "after":
             replay(mode)
             bitmap_and_combine()
@@ -1456,15 +1458,24 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
 
     mode_ms = {}
     reported = CFG4_REPORTED
+    # Across ranks the reported exchange is the fused peer-memory kernel beside the layers
+    # (build, exchange and AND in one launch over NVLink); NCCL (all-gather + AND kernel
+    # after the layers) is timed beside it.  One rank, or no symmetric memory: NCCL form.
+    exchange = "peer" if peer is not None else "beside"
+
+    def peer_alone():
+        peer.combine(projection.counts(candidate, out=peer_counts), refs, mapped_bits, out=peer_bits)
+
     with ClockSampler(dist.local_rank) as clocks:
         for mode in modes:
-            mode_ms[mode] = timed(lambda: step(mode), steps, warmup, dist) / steps
+            mode_ms[mode] = timed(lambda: step(mode, combine=exchange), steps, warmup, dist) / steps
         after_ms = timed(lambda: step(reported, combine="after"), steps, warmup, dist) / steps
         second_stream_ms = timed(lambda: step(reported, combine="second_stream"), steps, warmup, dist) / steps
         without_combine_ms = timed(lambda: replay(reported), steps, warmup, dist) / steps
         combine_alone_ms = timed(bitmap_and_combine, steps, warmup, dist) / steps
         layer_gather_ms = timed(lambda: replay("multi_layer_gather"), steps, warmup, dist) / steps
-        peer_ms = timed(lambda: step(reported, combine="peer"), steps, warmup, dist) / steps if peer else None
+        nccl_ms = timed(lambda: step(reported, combine="beside"), steps, warmup, dist) / steps
+        peer_alone_ms = timed(peer_alone, steps, warmup, dist) / steps if peer is not None else None
     torch.cuda.synchronize()
     expected_joint = bitmap_to_chunks(bits_buf)
     for r in range(dist.world):
@@ -1472,10 +1483,9 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
     joint_ok = bitmap_to_chunks(joint["bits"]) == expected_joint
     peer_record = {}
     if peer is not None:
-        peer_record = {"step_with_peer_combine_beside_ms": peer_ms,
-                       "peer_combine_matches_intersection": bitmap_to_chunks(peer_bits) == expected_joint and not peer.failed(),
-                       "peer_combine": "counts + ekv_freeable_and_peers (build + exchange + AND in one kernel "
-                                       "over NVLink peer memory) on the second stream beside the layers"}
+        peer_ok = bitmap_to_chunks(peer_bits) == expected_joint and not peer.failed()
+        joint_ok = joint_ok and peer_ok
+        peer_record = {"peer_alone_us": peer_alone_ms * 1e3, "peer_combine_matches_intersection": peer_ok}
     elif peer_error:
         peer_record = {"peer_combine_unavailable": peer_error}
     ms_per_step = mode_ms[reported]
@@ -1527,20 +1537,28 @@ def config4_leg(args, dist: Dist, steps: int, warmup: int):
                      "note": f"step = {layers} lookups + {layers} two-plane gathers + bitmap build + combine; "
                              "bytes = hit rows x 4 x row_bytes (K and V read and written) + miss rows x 2 x "
                              "row_bytes (zero rows written) + 13 B per lookup + 4 B per miss-list entry"},
-        "combine": {"what": ("freeable-bitmap build (counts + bitmap kernels) on a second stream beside the "
+        "combine": {"what": ("counts kernel + ekv_freeable_and_peers (this rank's bitmap built, published "
+                             "to every peer and ANDed with theirs over NVLink peer memory in one single-block "
+                             "kernel, bounded polls) on a second stream beside the layers"
+                             if exchange == "peer" else
+                             "freeable-bitmap build (counts + bitmap kernels) on a second stream beside the "
                              "layers, then NCCL all_gather_into_tensor of each rank's 512 B bitmap + AND kernel "
                              "after them"
                              if dist.world > 1 else "freeable-bitmap build (counts + bitmap kernels) on a second "
                                                     "stream beside the layers, single rank (no exchange)"),
-                    "alone_us": combine_alone_ms * 1e3,
+                    "alone_us": (peer_alone_ms if exchange == "peer" else combine_alone_ms) * 1e3,
                     "us_added_to_step": (ms_per_step - without_combine_ms) * 1e3,
                     "step_without_combine_ms": without_combine_ms,
-                    "step_with_build_and_exchange_after_the_layers_ms": after_ms,
-                    "step_with_combine_on_second_stream_ms": second_stream_ms,
+                    "step_with_nccl_exchange_after_the_layers_ms": nccl_ms,
+                    "nccl_alone_us": combine_alone_ms * 1e3,
+                    "step_with_build_and_nccl_exchange_after_the_layers_ms": after_ms,
+                    "step_with_nccl_combine_on_second_stream_ms": second_stream_ms,
                     "freeable_joint": len(bitmap_to_chunks(joint["bits"])),
                     "joint_matches_intersection": bool(joint_ok), **peer_record},
         "parity_layer0_and_last": bool(parity),
-        "gpu_launches": (2 * layers + 2) * steps + steps * (dist.world > 1),
+        # per step: 48 fused launches + 48 compactions + counts + (bitmap, or the fused
+        # exchange kernel); the NCCL form adds the AND kernel across ranks
+        "gpu_launches": (2 * layers + 2) * steps + steps * (dist.world > 1 and exchange != "peer"),
         "clocks": clocks.summary(),
     }
     graphs.clear()
