@@ -506,7 +506,7 @@ REFERENCE_ROUND_TRIP = dict(bytes=503_347_200, seconds=0.1314, gbs=3.8,
                             source="results/vmm-roundtrip-shadow/results.json:699-700 (4x A100, TP4, per rank)")
 
 
-def round_trip_bench(dev, reps=3, spare_chunks=0):
+def round_trip_bench(dev, reps=5, spare_chunks=0):
     """A forced demote + promote round trip through the reference's transaction API
     (prepare_demote -> commit_demote -> prepare_promote -> commit_promote,
     adaptive_sparse/migration.py:67-288) on one TP4 rank's shard: 48 layers x K,V of
