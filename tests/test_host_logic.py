@@ -516,6 +516,28 @@ def test_no_cpu_fallback_without_cuda_tensors():
         lookup_slots(torch.zeros((2, 4), dtype=torch.int32), torch.zeros((2, 3), dtype=torch.int32))
 
 
+def test_lookup_gather_has_no_cpu_fallback():
+    """The fused lookup + gather rejects host tensors before any launch, and rejects
+    mismatched shapes first."""
+    from ekv_b200.sparse_read import LookupGather
+    from ekv_b200.virtual_layout import VirtualKVLayout
+
+    layout = VirtualKVLayout(2, 8, 16, itemsize=2, chunk_bytes=4096)
+    plane = torch.zeros(layout.capacity_bytes // 2, dtype=torch.int16)
+    res_map = torch.full((2, 20), -1, dtype=torch.int32)
+    topk = torch.zeros((2, 5), dtype=torch.int32)
+    ids, lengths = torch.arange(2), torch.full((2,), 20)
+    out = torch.empty((2, 5, 16), dtype=torch.int16)
+    with pytest.raises(ValueError, match="CUDA"):
+        LookupGather([plane], res_map, topk, ids, lengths, [out], layout, disjoint=True)
+    with pytest.raises(ValueError, match="output shape"):
+        LookupGather([plane], res_map, topk, ids, lengths, [out[:, :4]], layout)
+    with pytest.raises(ValueError, match="one entry per Top-K row"):
+        LookupGather([plane], res_map, topk, ids[:1], lengths, [out], layout)
+    with pytest.raises(ValueError, match="EKV_MAX_PLANES"):
+        LookupGather([], res_map, topk, ids, lengths, [], layout)
+
+
 def test_library_missing_fails_loudly(tmp_path):
     from ekv_b200 import _lib
 
