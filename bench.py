@@ -10,7 +10,7 @@ Under ``--gpus N`` (torchrun) the KV heads are sharded across ranks
 fixed: ``scaling = strong``.  One step = one launch over the whole batch.
 
 Extra keys: ``e2e`` (public Python API per step, positions copied from pinned
-host memory and one result row read back), ``roofline`` (gather kernel vs the
+host memory -- one step ahead, on a second stream -- and one result row read back), ``roofline`` (gather kernel vs the
 measured HBM copy peak), ``cpu_baseline`` (torch-CPU restatement on the host
 cores, bounded sample), ``migration`` (config 3: 256 victim chunks packed into
 pinned host staging through the copy-engine ring and restored into fresh VMM
@@ -28,8 +28,9 @@ region).
 
 ``config4``: config 4 (BASELINE.json's 2/4/8-GPU configuration) measured in the
 same run after the config-2 pool is released: 48 layers of lookup + K,V gather per
-decode step, then the freeable-bitmap build and its cross-rank AND-combine, all
-inside the timed step (``--skip-config4`` leaves it out).  ``config5``, on one GPU:
+decode step and the freeable bitmap with its cross-rank AND-combine (for N > 1 one
+kernel over NVLink peer memory beside the layers; NCCL all-gather + AND after them
+timed beside it), all inside the timed step (``--skip-config4`` leaves it out).  ``config5``, on one GPU:
 config 5's 64 decode steps (lookup -> victim selection -> promotion from pinned host
 history -> gather per layer), as ``--config 5`` reports them (``--skip-config5``).
 
