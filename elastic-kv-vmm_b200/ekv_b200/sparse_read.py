@@ -4,7 +4,9 @@
 experimental/sparse_read.py:33-51.  ``gather_rows_planes`` applies one row
 selection to many planes (every layer's K and V) in a single launch, resolving
 the index chain once per row; it is the form the decode path and the benchmark
-use.
+use.  ``PlaneGather`` pre-binds it for a decode loop, ``LookupGather`` runs a
+layer's residency lookup inside its mapped gather, and ``LayerGather`` gathers
+every layer's own selection in one launch.
 """
 
 from __future__ import annotations
